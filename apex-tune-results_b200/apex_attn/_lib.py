@@ -1,0 +1,82 @@
+"""ctypes binding of the C ABI declared in include/apex_attn.h.
+
+The shared library is built in-tree next to this file (``libapex_attn.so``) by
+``apex-tune-results_b200/build.py``. There is no fallback: if the library is missing the
+import of :mod:`apex_attn` still works, but every call raises ``RuntimeError`` naming
+the missing file, so a CUDA-less or stale checkout fails loudly instead of silently
+computing attention some other way.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_NAME = "libapex_attn.so"
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+
+# Status codes, mirrored from include/apex_attn.h.
+OK = 0
+ERR_INVALID_ARGUMENT = -1
+ERR_UNSUPPORTED_HEAD_DIM = -2
+ERR_UNSUPPORTED_DTYPE = -3
+ERR_BAD_LAYOUT = -4
+ERR_BAD_SCALE = -5
+ERR_NO_DEVICE = -6
+ERR_UNSUPPORTED_ARCH = -7
+ERR_TENSOR_MAP = -8
+ERR_LAUNCH = -9
+ERR_DEVICE_TIMEOUT = -10
+ERR_TOO_LARGE = -11
+ERR_CUDA = -12
+
+DTYPE_BF16 = 0
+DTYPE_FP16 = 1
+
+# Every symbol the header declares: (name, restype, argtypes).
+_c_ll_p = ctypes.POINTER(ctypes.c_longlong)
+SYMBOLS = {
+    "apex_attn_fwd": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+         ctypes.c_float, _c_ll_p, ctypes.c_void_p],
+    ),
+    "apex_attn_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "apex_attn_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p]),
+    "apex_attn_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "apex_attn_version": (ctypes.c_int, []),
+    "apex_attn_supports_head_dim": (ctypes.c_int, [ctypes.c_int]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads (once) and returns the library with argtypes configured."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"apex_attn native library not found at {LIB_PATH}; build it with "
+                    "`python apex-tune-results_b200/build.py` (there is no non-CUDA fallback)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SYMBOLS.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def strerror(code: int) -> str:
+    return load().apex_attn_strerror(int(code)).decode()
+
+
+def check(code: int, what: str = "apex_attn") -> None:
+    if code != OK:
+        raise RuntimeError(f"{what} failed: {strerror(code)} (status {code})")

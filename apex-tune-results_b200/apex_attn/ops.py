@@ -1,0 +1,96 @@
+"""The operator surface of mls-bench_fused_attention, backed by the sm_100a kernel.
+
+``custom_attention_forward(q, k, v, causal=True, sm_scale=None)`` has the signature,
+defaults, output and error behaviour of the reference operator
+(mls-bench_fused_attention/fused_attention.py:155-193; spec comment submission.py:20-26):
+
+* q, k, v: ``[batch, nheads, seqlen, headdim]`` CUDA tensors, fp16 or bf16;
+* ``sm_scale`` defaults to ``1/sqrt(headdim)`` (fused_attention.py:158-159);
+* an unsupported ``headdim`` raises ``KeyError(headdim)``, as ``_CONFIGS[headdim]`` does
+  (fused_attention.py:162);
+* the result is a new contiguous tensor of q's shape and dtype, produced asynchronously
+  on the current CUDA stream (fused_attention.py:161).
+
+Extension beyond the reference: ``return_lse=True`` also returns the fp32 natural-log
+logsumexp ``[batch, nheads, seqlen]``. Inputs whose layout the TMA tensor maps accept
+directly (unit head-dim stride, other strides multiples of 8 elements) are not copied;
+others are made contiguous first, like the reference's ``.contiguous()`` (:157).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_FP16}
+
+
+def supports_head_dim(headdim: int) -> bool:
+    return bool(_lib.load().apex_attn_supports_head_dim(int(headdim)))
+
+
+def _tma_ready(t: torch.Tensor) -> torch.Tensor:
+    if t.stride(-1) != 1 or t.data_ptr() % 16 != 0:
+        return t.contiguous()
+    for size, stride in zip(t.shape[:3], t.stride()[:3]):
+        if size > 1 and stride % 8 != 0:
+            return t.contiguous()
+    return t
+
+
+def _strides(t: torch.Tensor) -> list[int]:
+    """(batch, head, seq) element strides; size-1 dims get their contiguous stride."""
+    b, h, n, d = t.shape
+    contiguous = (h * n * d, n * d, d)
+    return [s if size > 1 else c for size, s, c in zip((b, h, n), t.stride()[:3], contiguous)]
+
+
+def custom_attention_forward(q, k, v, causal=True, sm_scale=None, return_lse=False):
+    """Causal (or full) attention forward on B200; see the module docstring."""
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q, k, v must share one [B, H, N, D] shape, got {tuple(q.shape)}, "
+                         f"{tuple(k.shape)}, {tuple(v.shape)}")
+    batch, nheads, seqlen, headdim = q.shape
+    if not supports_head_dim(headdim):
+        raise KeyError(headdim)
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError(f"q, k, v must all be float16 or bfloat16, got {q.dtype}, {k.dtype}, {v.dtype}")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda) or not (q.device == k.device == v.device):
+        raise ValueError("q, k, v must be CUDA tensors on one device")
+    q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(headdim)
+    o = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    lse = torch.empty((batch, nheads, seqlen), dtype=torch.float32, device=q.device) if return_lse else None
+    if q.numel() == 0:
+        return (o, lse) if return_lse else o
+    strides = (ctypes.c_longlong * 12)(*(_strides(q) + _strides(k) + _strides(v) + _strides(o)))
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = _lib.load().apex_attn_fwd(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+        lse.data_ptr() if lse is not None else None,
+        batch, nheads, seqlen, headdim, _DTYPES[q.dtype], 1 if causal else 0, float(sm_scale),
+        strides, stream)
+    _lib.check(rc, "custom_attention_forward")
+    return (o, lse) if return_lse else o
+
+
+def device_status(device: int | None = None) -> int:
+    """Synchronises `device`, returns and clears its status bits (0 = no kernel fault)."""
+    if device is None:
+        device = torch.cuda.current_device()
+    flags = ctypes.c_int(0)
+    rc = _lib.load().apex_attn_device_status(int(device), ctypes.byref(flags))
+    if rc not in (_lib.OK, _lib.ERR_DEVICE_TIMEOUT):
+        _lib.check(rc, "apex_attn_device_status")
+    return int(flags.value)
+
+
+def selftest_wait_timeout(timeout_us: int = 1000) -> None:
+    """Launches the bounded-wait self-test kernel on the current stream."""
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(_lib.load().apex_attn_selftest_wait_timeout(int(timeout_us), stream),
+               "apex_attn_selftest_wait_timeout")

@@ -1,0 +1,302 @@
+// Host side of apex_attn: argument validation, tensor-map encoding, per-device state
+// and kernel dispatch behind the C ABI declared in include/apex_attn.h.
+//
+// The Python operator custom_attention_forward (mls-bench_fused_attention/
+// fused_attention.py:155-193) did, per call: make q/k/v contiguous, default the scale,
+// fold log2(e), allocate o, pick a per-head-dim config (_CONFIGS, :148-152), build TMA
+// descriptors for d=128 (:165-169) and launch a grid of (ceil(N/128), B*H) programs.
+// Here the caller owns every buffer; this file validates the layout, encodes 4-D TMA
+// tensor maps (so strided [B,H,N,D] and [B,N,H,D] views need no copy), and launches one
+// persistent CTA per SM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <mutex>
+
+#include "apex_attn.h"
+#include "attn_fwd_kernel.cuh"
+
+namespace {
+
+using apex::AttnParams;
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kMaxDevices = 64;
+constexpr int kStatusBytes = 256;
+
+struct DeviceState {
+  bool ready = false;
+  int* status = nullptr;
+  int num_sms = 0;
+  int cc_major = 0, cc_minor = 0;
+  unsigned attr_done = 0;  // bit per kernel instantiation
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+bool g_encode_tried = false;
+
+unsigned long long wait_timeout_ns() {
+  static const unsigned long long v = [] {
+    const char* s = std::getenv("APEX_ATTN_WAIT_TIMEOUT_MS");
+    long long ms = s ? std::atoll(s) : 0;
+    if (ms <= 0) ms = 2000;
+    return (unsigned long long)ms * 1000000ull;
+  }();
+  return v;
+}
+
+int init_device(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= kMaxDevices) return APEX_ATTN_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode_tried) {
+    g_encode_tried = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) ==
+            cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    else
+      (void)cudaGetLastError();
+  }
+  if (g_encode == nullptr) return APEX_ATTN_ERR_TENSOR_MAP;
+  DeviceState& s = g_dev[dev];
+  if (!s.ready) {
+    if (cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&s.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&s.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_NO_DEVICE;
+    }
+    if (s.cc_major != 10 || s.cc_minor != 0) return APEX_ATTN_ERR_UNSUPPORTED_ARCH;
+    if (cudaMalloc(&s.status, kStatusBytes) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_CUDA;
+    }
+    if (cudaMemset(s.status, 0, kStatusBytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_CUDA;
+    }
+    s.ready = true;
+  }
+  *out = &s;
+  return APEX_ATTN_OK;
+}
+
+// Resolves the device that owns `ptr`; -1 when it is not device memory.
+int device_of(const void* ptr) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -1;
+  }
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) return -1;
+  return a.device;
+}
+
+// 4-D tiled map over a logical [B, H, N, D] tensor, dims ordered (D, N, H, B), box
+// (64, 128, 1, 1), 128-byte swizzle, zero fill out of bounds (rows >= N read as 0).
+int encode_map(CUtensorMap* m, const void* ptr, int dtype, int B, int H, int N, int D, long long sb,
+               long long sh, long long sn) {
+  // Strides of size-1 dims are never used; give them a legal value.
+  if (H == 1) sh = (long long)N * sn;
+  if (B == 1) sb = (long long)H * sh;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)sn * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)apex::kBlockM, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(m, dtype == APEX_ATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        4, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? APEX_ATTN_OK : APEX_ATTN_ERR_TENSOR_MAP;
+}
+
+template <int D, typename T, int NS>
+int launch(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
+           const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
+  auto kern = apex::attn_fwd_sm100_kernel<D, T, NS>;
+  constexpr int smem = apex::SmemPlan<D, NS>::kDynamicBytes;
+  if (!(ds.attr_done & attr_bit)) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_LAUNCH;
+    }
+    ds.attr_done |= attr_bit;
+  }
+  kern<<<grid, apex::kThreads, smem, stream>>>(mq, mk, mv, p);
+  if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
+  return APEX_ATTN_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      prev = -1;
+    }
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+__global__ void wait_timeout_selftest_kernel(int* status, unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    apex::ptx::mbar_init(apex::ptx::smem_u32(&bar), 1);
+    abort_flag = 0;
+    apex::ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const apex::Waiter w{&abort_flag, status, timeout_ns};
+    (void)w.wait(apex::ptx::smem_u32(&bar), 0);  // nothing ever arrives: must time out
+  }
+  __syncthreads();
+}
+
+}  // namespace
+
+extern "C" {
+
+int apex_attn_version(void) { return kVersion; }
+
+int apex_attn_supports_head_dim(int head_dim) { return (head_dim == 64 || head_dim == 128) ? 1 : 0; }
+
+const char* apex_attn_strerror(int status) {
+  switch (status) {
+    case APEX_ATTN_OK: return "success";
+    case APEX_ATTN_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer or non-positive size)";
+    case APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM: return "unsupported head dim (supported: 64, 128)";
+    case APEX_ATTN_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (supported: bf16, fp16)";
+    case APEX_ATTN_ERR_BAD_LAYOUT: return "layout not supported: head-dim stride must be 1, other strides multiples of 8 elements, pointers 16-byte aligned";
+    case APEX_ATTN_ERR_BAD_SCALE: return "sm_scale must be finite and > 0";
+    case APEX_ATTN_ERR_NO_DEVICE: return "tensors are not CUDA device memory on one device";
+    case APEX_ATTN_ERR_UNSUPPORTED_ARCH: return "device is not sm_100 (B200)";
+    case APEX_ATTN_ERR_TENSOR_MAP: return "TMA tensor map encoding failed";
+    case APEX_ATTN_ERR_LAUNCH: return "kernel launch failed";
+    case APEX_ATTN_ERR_DEVICE_TIMEOUT: return "a kernel hit its bounded-wait limit (device status set)";
+    case APEX_ATTN_ERR_TOO_LARGE: return "sizes exceed the supported range";
+    case APEX_ATTN_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
+                  int heads, int seqlen, int head_dim, int dtype, int causal, float sm_scale,
+                  const long long* strides, void* stream) {
+  // ---- argument validation (no CUDA calls) ----
+  if (!q || !k || !v || !o || !strides) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || heads <= 0 || seqlen <= 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (!apex_attn_supports_head_dim(head_dim)) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
+  if (dtype != APEX_ATTN_BF16 && dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
+  if (!std::isfinite(sm_scale) || !(sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
+  const long long BH = (long long)batch * heads;
+  const long long mblocks = (seqlen + apex::kItemRows - 1) / apex::kItemRows;
+  if (BH * mblocks > 0x7fffffffLL || seqlen > (1 << 30) || BH > (1LL << 30)) return APEX_ATTN_ERR_TOO_LARGE;
+  for (int i = 0; i < 12; ++i)
+    if (strides[i] < 0 || (strides[i] & 7) != 0 || strides[i] >= (1LL << 38)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  for (int t = 0; t < 4; ++t)
+    if (strides[3 * t + 2] < head_dim) return APEX_ATTN_ERR_BAD_LAYOUT;  // rows must not overlap
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  if (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)) return APEX_ATTN_ERR_BAD_LAYOUT;
+
+  // ---- device ----
+  const int dev = device_of(q);
+  if (dev < 0 || device_of(k) != dev || device_of(v) != dev || device_of(o) != dev) return APEX_ATTN_ERR_NO_DEVICE;
+  if (lse && device_of(lse) != dev) return APEX_ATTN_ERR_NO_DEVICE;
+  DeviceGuard guard(dev);
+  DeviceState* ds = nullptr;
+  int rc = init_device(dev, &ds);
+  if (rc != APEX_ATTN_OK) return rc;
+
+  CUtensorMap mq, mk, mv;
+  if ((rc = encode_map(&mq, q, dtype, batch, heads, seqlen, head_dim, strides[0], strides[1], strides[2])) ||
+      (rc = encode_map(&mk, k, dtype, batch, heads, seqlen, head_dim, strides[3], strides[4], strides[5])) ||
+      (rc = encode_map(&mv, v, dtype, batch, heads, seqlen, head_dim, strides[6], strides[7], strides[8])))
+    return rc;
+
+  AttnParams p{};
+  p.o = o;
+  p.lse = lse;
+  p.status = ds->status;
+  p.o_sb = strides[9];
+  p.o_sh = strides[10];
+  p.o_sn = strides[11];
+  p.B = batch;
+  p.H = heads;
+  p.N = seqlen;
+  p.num_mblocks = (int)mblocks;
+  p.num_kblocks = (seqlen + apex::kBlockN - 1) / apex::kBlockN;
+  p.num_items = (int)(BH * mblocks);
+  // Heads per scheduling group: keep the K/V of the heads that concurrently running CTAs
+  // stream within ~48 MB of L2.
+  const double kv_bytes_per_head = 2.0 * seqlen * head_dim * 2.0;
+  long long g = (long long)(48.0 * 1024 * 1024 / kv_bytes_per_head);
+  p.group_heads = (int)std::max(1LL, std::min(g, BH));
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.causal = causal ? 1 : 0;
+  p.timeout_ns = wait_timeout_ns();
+  const int grid = std::min(p.num_items, ds->num_sms);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  if (head_dim == 64) {
+    if (dtype == APEX_ATTN_BF16) return launch<64, __nv_bfloat16, 8>(*ds, 1u, mq, mk, mv, p, grid, s);
+    return launch<64, __half, 8>(*ds, 2u, mq, mk, mv, p, grid, s);
+  }
+  if (dtype == APEX_ATTN_BF16) return launch<128, __nv_bfloat16, 4>(*ds, 4u, mq, mk, mv, p, grid, s);
+  return launch<128, __half, 4>(*ds, 8u, mq, mk, mv, p, grid, s);
+}
+
+int apex_attn_device_status(int device, int* flags) {
+  if (!flags) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(device);
+  DeviceState* ds = nullptr;
+  int rc = init_device(device, &ds);
+  if (rc != APEX_ATTN_OK) return rc;
+  int host[1] = {0};
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_CUDA;
+  }
+  if (cudaMemcpy(host, ds->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess ||
+      cudaMemset(ds->status, 0, sizeof(int)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_CUDA;
+  }
+  *flags = host[0];
+  return host[0] ? APEX_ATTN_ERR_DEVICE_TIMEOUT : APEX_ATTN_OK;
+}
+
+int apex_attn_selftest_wait_timeout(int timeout_us, void* stream) {
+  if (timeout_us <= 0 || timeout_us > 10 * 1000 * 1000) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_NO_DEVICE;
+  }
+  DeviceState* ds = nullptr;
+  int rc = init_device(dev, &ds);
+  if (rc != APEX_ATTN_OK) return rc;
+  wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      ds->status, (unsigned long long)timeout_us * 1000ull);
+  if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
+  return APEX_ATTN_OK;
+}
+
+}  // extern "C"

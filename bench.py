@@ -1,0 +1,381 @@
+"""Benchmark of the B200 causal attention forward (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {apex,reference}]
+
+N = 1: the BASELINE.json headline workload C3 (B=4, H=32, N=8192, d=128, bf16, causal,
+with the fp32 logsumexp), plus C2 (d=64) and C4 (d=256, once built) as extra entries.
+A "step" is one forward over the whole batch. value = causal FLOP (2*B*H*N^2*d,
+submission.py:235-240) per second over the K timed steps, device-timed with CUDA events,
+inputs resident in HBM (q/k/v = 805 MB, larger than the 126 MB L2, so no flush).
+
+N > 1 (torchrun, one rank per GPU): C5 (B=8, H=64, N=16384, d=128) with batch x heads
+sharded over the ranks (strong scaling, no collective in the timed region), the output
+gathered to rank 0 over NCCL afterwards and spot-checked there.
+
+--impl reference: the reference's own math path on the host CPU (torch SDPA in fp32,
+submission.py:223-232, restated in oracle/attention_oracle.py) over a bounded sample of
+heads of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "apex-tune-results_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "causal attn fwd TFLOP/s at d=64/128/256; % of B200 BF16 dense peak"
+CONFIGS = {
+    "C2": dict(B=4, H=16, N=4096, D=64),
+    "C3": dict(B=4, H=32, N=8192, D=128),
+    "C4": dict(B=2, H=16, N=8192, D=256),
+    "C5": dict(B=8, H=64, N=16384, D=128),
+}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def flops(c) -> float:
+    return 2.0 * c["B"] * c["H"] * c["N"] ** 2 * c["D"]
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return FALLBACK_PEAKS, "fallback"
+
+
+# --------------------------------------------------------------------- clocks --
+class ClockSampler:
+    """Polls NVML (SM clock, clock-event reasons) every few ms in a thread."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples = []
+        self.period = period_s
+        self.ok = False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # pragma: no cover - depends on the box
+            self.err = repr(e)
+            self.max_mhz = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM)
+                rs = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self.ok:
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "nvml unavailable"}
+        loaded = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        reasons = set()
+        for _, rs in loaded:
+            for bit, name in self.REASONS.items():
+                if rs & bit and bit != 0x1:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median([s[0] for s in loaded]) if loaded else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons), "samples": len(loaded)}
+
+
+# ------------------------------------------------------------------ workloads --
+def make_device_inputs(c, seed, device, heads=None):
+    """Seeded N(0,1) bf16 inputs generated on the device (same values on every B200)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, H, N, D = c["B"], c["H"], c["N"], c["D"]
+    shape = (B, H, N, D) if heads is None else (heads, 1, N, D)
+    q = torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+    k = torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+    v = torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+    return q, k, v
+
+
+def time_device(fn, steps, warmup, stream):
+    """Warm-up, then K steps bracketed by synchronize; returns (total_ms, per-launch ms)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        ev[i][0].record(stream)
+        fn()
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1), [a.elapsed_time(b) for a, b in ev]
+
+
+def bench_config(name, c, steps, warmup, device):
+    from apex_attn import custom_attention_forward
+    stream = torch.cuda.current_stream(device)
+    q, k, v = make_device_inputs(c, 42, device)
+    fn = lambda: custom_attention_forward(q, k, v, causal=True, return_lse=(name == "C3"))
+    total_ms, per = time_device(fn, steps, warmup, stream)
+    f = flops(c)
+    return {"tflops": f * steps / (total_ms * 1e-3) / 1e12, "ms_per_step": total_ms / steps,
+            "kernel_ms_median": statistics.median(per), "kernel_ms_mean": sum(per) / len(per),
+            "flop_per_step": f}
+
+
+def bench_e2e(c, steps, warmup, device):
+    """Same metric through the public API with host buffers: each step copies q/k/v from
+    pinned host memory to the device, runs the forward and copies o and lse back."""
+    from apex_attn import custom_attention_forward
+    stream = torch.cuda.current_stream(device)
+    qd, kd, vd = make_device_inputs(c, 42, device)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (qd, kd, vd))
+    del qd, kd, vd
+    ho = torch.empty(hq.shape, dtype=hq.dtype).pin_memory()
+    hl = torch.empty(hq.shape[:3], dtype=torch.float32).pin_memory()
+
+    def step():
+        q = hq.to(device, non_blocking=True)
+        k = hk.to(device, non_blocking=True)
+        v = hv.to(device, non_blocking=True)
+        o, lse = custom_attention_forward(q, k, v, causal=True, return_lse=True)
+        ho.copy_(o, non_blocking=True)
+        hl.copy_(lse, non_blocking=True)
+
+    total_ms, _ = time_device(step, steps, warmup, stream)
+    bi = 3 * hq.numel() * hq.element_size()
+    bo = ho.numel() * ho.element_size() + hl.numel() * 4
+    return {"value": flops(c) * steps / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": total_ms / steps}
+
+
+def cpu_reference(c, budget_s=12.0, max_heads=None):
+    """The reference math path (torch SDPA fp32, submission.py:223-232) on the host over a
+    bounded sample of heads of workload `c`. Returns (TFLOP/s, cores, sample text)."""
+    from oracle.attention_oracle import reference_attention_cpu
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    g = torch.Generator().manual_seed(42)
+    N, D = c["N"], c["D"]
+    q = torch.randn((1, 1, N, D), generator=g).to(torch.bfloat16).float()
+    k = torch.randn((1, 1, N, D), generator=g).to(torch.bfloat16).float()
+    v = torch.randn((1, 1, N, D), generator=g).to(torch.bfloat16).float()
+    reference_attention_cpu(q[..., :256, :], k[..., :256, :], v[..., :256, :])  # warm-up
+    heads = 0
+    t0 = time.perf_counter()
+    limit = max_heads or c["B"] * c["H"]
+    while heads < limit and (time.perf_counter() - t0) < budget_s:
+        reference_attention_cpu(q, k, v, causal=True)
+        heads += 1
+    dt = time.perf_counter() - t0
+    f = 2.0 * N * N * D * heads
+    sample = f"{heads} of {c['B'] * c['H']} (b,h) heads at N={N}, d={D}, fp32 SDPA, {dt:.1f} s"
+    return f / dt / 1e12, cores, sample
+
+
+
+def shard_inputs(c, h0, h1, device, seed=42):
+    """bf16 q/k/v of flattened heads [h0, h1) as a [1, h1-h0, N, D] tensor; seeded by the
+    shard start so any rank can regenerate any shard."""
+    g = torch.Generator(device=device).manual_seed(seed * 1000003 + h0)
+    shape = (1, h1 - h0, c["N"], c["D"])
+    return tuple(torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+                 for _ in range(3))
+
+
+def run_multi(args, c, rank, world, local_rank):
+    """C5 over `world` GPUs: each rank runs the kernel on its b*h shard, timed on the
+    device, max over ranks; the output is gathered to rank 0 (NCCL) after timing and a
+    sample of heads is checked there against the fp32 reference."""
+    import datetime
+
+    import torch.distributed as dist
+    from apex_attn import custom_attention_forward, device_status
+    from apex_attn.shard import gather_to_rank0, shard_heads
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    try:
+        total = c["B"] * c["H"]
+        h0, h1 = shard_heads(total, world, rank)
+        q, k, v = shard_inputs(c, h0, h1, device)
+        stream = torch.cuda.current_stream(device)
+        fn = lambda: custom_attention_forward(q, k, v, causal=True)
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(local_rank) as clk:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            t1.record(stream)
+            torch.cuda.synchronize()
+        dist.barrier()
+        ms = torch.tensor([t0.elapsed_time(t1)], device=device)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        tmax = ms.item()
+        o = fn()
+        status = device_status(local_rank)
+        full = gather_to_rank0(o.reshape(h1 - h0, c["N"], c["D"]), total, world, rank)
+        if rank == 0:
+            sys.path.insert(0, os.path.join(ROOT, "tests"))
+            import gpu_ref
+            err = 0.0
+            for r in (0, world - 1):
+                s0, s1 = shard_heads(total, world, r)
+                rq, rk, rv = shard_inputs(c, s0, s1, device)
+                sel = slice(0, 2)
+                ro, _ = gpu_ref.attention_fp32(rq[:, sel], rk[:, sel], rv[:, sel], causal=True, with_lse=False)
+                err = max(err, (full[s0:s0 + 2].float() - ro[0]).abs().max().item())
+            value = flops(c) * args.steps / (tmax * 1e-3) / 1e12
+            peaks, peak_kind = load_peaks()
+            line = {
+                "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": tmax / args.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,1), device RNG)",
+                "config": {"workload": "C5: causal attn fwd B=8 H=64 N=16384 d=128 bf16, b*h sharded",
+                           "global_batch": c["B"], "seq_len": c["N"], "heads": c["H"], "head_dim": c["D"],
+                           "parallelism": f"dp{world} over b*h", "heads_per_rank": h1 - h0},
+                "frac_of_peak_per_gpu": value / world / peaks["bf16_tflops"],
+                "gpu_launches": args.steps,
+                "clocks": clk.summary(),
+                "parity": {"max_abs_err_sampled_heads": err, "tol": 1e-2},
+                "device_status": status,
+            }
+            print(json.dumps(line))
+        del full
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------- main --
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["apex", "reference"], default="apex")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        c = CONFIGS["C3"] if args.gpus == 1 else CONFIGS["C5"]
+        vals = []
+        for _ in range(max(1, min(args.steps, 3))):
+            v, cores, sample = cpu_reference(c, budget_s=args.cpu_budget / 2)
+            vals.append(v)
+        value = statistics.median(vals)
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": ("C3 " if args.gpus == 1 else "C5 ") + json.dumps(c)},
+                "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "vs_baseline": None}
+        print(json.dumps(line))
+        return
+
+    if args.gpus > 1 or world > 1:
+        run_multi(args, CONFIGS["C5"], rank, world, local_rank)
+        return
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    import apex_attn
+    peaks, peak_kind = load_peaks()
+    c3 = CONFIGS["C3"]
+    with ClockSampler(0) as clk:
+        res = bench_config("C3", c3, args.steps, args.warmup, device)
+    clocks = clk.summary()
+    extra = {}
+    for name in ("C2", "C4"):
+        c = CONFIGS[name]
+        if apex_attn.supports_head_dim(c["D"]):
+            r = bench_config(name, c, args.steps, args.warmup, device)
+            extra[name] = {"tflops": round(r["tflops"], 1), "ms_per_step": round(r["ms_per_step"], 4),
+                           "frac_of_peak": round(r["tflops"] / peaks["bf16_tflops"], 4),
+                           "config": c}
+        else:
+            extra[name] = {"tflops": None, "note": f"head dim {c['D']} not built"}
+    e2e = bench_e2e(c3, max(3, min(args.steps, 10)), 3, device)
+    status = apex_attn.device_status()
+    cpu_v, cores, sample = cpu_reference(c3, budget_s=args.cpu_budget)
+    peak = peaks["bf16_tflops"]
+    achieved = res["flop_per_step"] / (res["kernel_ms_mean"] * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": res["tflops"], "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1), device RNG)",
+        "config": {"workload": "C3: causal attn fwd B=4 H=32 N=8192 d=128 bf16 + fp32 lse",
+                   "global_batch": c3["B"], "seq_len": c3["N"], "heads": c3["H"], "head_dim": c3["D"],
+                   "parallelism": "single GPU", "l2": "inputs 805 MB > 126 MB L2, no flush"},
+        "frac_of_peak": res["tflops"] / peak,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "peak_source": f"{peak_kind} bf16_tflops (MEASURED_PEAKS.json)"},
+        "cpu_baseline": {"value": cpu_v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "per_config": extra,
+        "device_status": status,
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,92 @@
+/*
+ * apex_attn — C ABI of the B200 (sm_100a) fused attention forward.
+ *
+ * This header is the drop-in boundary for the operator
+ *   custom_attention_forward(q, k, v, causal=True, sm_scale=None) -> o
+ * of mls-bench_fused_attention/fused_attention.py:155-193 (identical copy at
+ * submission.py:179-217). The Python host module `apex_attn` binds it with ctypes;
+ * any other FFI binds the same symbols.
+ *
+ * Conventions: all pointers are device pointers on one CUDA device, tensors are
+ * logical [B, H, N, D] with unit stride along D, strides are given in elements.
+ * Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy default
+ * stream). No call allocates caller-visible memory; the library keeps one small
+ * status word per device for device-side error reporting.
+ */
+#ifndef APEX_ATTN_H_
+#define APEX_ATTN_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (returned by every entry point; 0 = success). */
+#define APEX_ATTN_OK 0
+#define APEX_ATTN_ERR_INVALID_ARGUMENT -1   /* null pointer, non-positive size */
+#define APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM -2
+#define APEX_ATTN_ERR_UNSUPPORTED_DTYPE -3
+#define APEX_ATTN_ERR_BAD_LAYOUT -4         /* stride/alignment not TMA-compatible */
+#define APEX_ATTN_ERR_BAD_SCALE -5          /* sm_scale not finite and > 0 */
+#define APEX_ATTN_ERR_NO_DEVICE -6          /* pointer not on a CUDA device / no device */
+#define APEX_ATTN_ERR_UNSUPPORTED_ARCH -7   /* device is not sm_100 */
+#define APEX_ATTN_ERR_TENSOR_MAP -8         /* cuTensorMapEncodeTiled rejected a tensor */
+#define APEX_ATTN_ERR_LAUNCH -9             /* kernel launch failed */
+#define APEX_ATTN_ERR_DEVICE_TIMEOUT -10    /* a kernel hit its bounded-wait limit */
+#define APEX_ATTN_ERR_TOO_LARGE -11         /* sizes exceed the supported range */
+#define APEX_ATTN_ERR_CUDA -12              /* other CUDA runtime error */
+
+/* Element types. */
+#define APEX_ATTN_BF16 0
+#define APEX_ATTN_FP16 1
+
+/*
+ * Causal (or full) attention forward:
+ *   o[b,h,i,:] = sum_j softmax_j(q[b,h,i,:] . k[b,h,j,:] * sm_scale) v[b,h,j,:]
+ * with j <= i when causal != 0. Accumulation is fp32; o has the input dtype.
+ * lse (nullable) receives the fp32 natural-log logsumexp of each row, contiguous
+ * [B, H, N].
+ *
+ * strides: 12 values, element strides (batch, head, seq) for q, k, v, o in that
+ * order. Each must be a multiple of 8 elements (16 bytes); pointers 16-byte aligned.
+ * head_dim: 64, 128 or 256 (fused_attention.py:148-152 covers the same three).
+ *
+ * Replaces: custom_attention_forward body, fused_attention.py:155-193, and the
+ * per-head-dim table _CONFIGS, fused_attention.py:148-152 (a KeyError there is
+ * APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM here).
+ */
+int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
+                  int heads, int seqlen, int head_dim, int dtype, int causal, float sm_scale,
+                  const long long* strides, void* stream);
+
+/*
+ * Reads and clears the device status word of `device` after synchronising that
+ * device. *flags receives the raw bits (1 = a kernel hit its bounded-wait limit).
+ * Returns APEX_ATTN_ERR_DEVICE_TIMEOUT when any bit was set.
+ * Has no counterpart in the reference (its Triton kernels cannot report device faults).
+ */
+int apex_attn_device_status(int device, int* flags);
+
+/*
+ * Launches a one-CTA kernel whose bounded wait on an mbarrier that nothing arrives
+ * on must expire after `timeout_us` microseconds, setting the device status bit.
+ * Used by the failure-detection test; it never faults or hangs the GPU.
+ * Has no counterpart in the reference.
+ */
+int apex_attn_selftest_wait_timeout(int timeout_us, void* stream);
+
+/* Human-readable text for a status code. Replaces the exception text the reference
+ * harness prints on failure (submission.py:299-306). */
+const char* apex_attn_strerror(int status);
+
+/* Library version as major*10000 + minor*100 + patch. */
+int apex_attn_version(void);
+
+/* 1 if head_dim is supported by apex_attn_fwd, else 0 (mirrors `headdim in _CONFIGS`,
+ * fused_attention.py:148-152). */
+int apex_attn_supports_head_dim(int head_dim);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* APEX_ATTN_H_ */

@@ -1,0 +1,101 @@
+"""C-ABI checks that need no GPU: the library loads, exports exactly what
+include/apex_attn.h declares, and rejects bad arguments with the documented codes
+before touching CUDA."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from apex_attn import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "apex_attn.h")
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(apex_attn_\w+)\s*\(", text, re.M)))
+
+
+def header_codes():
+    text = open(HEADER).read()
+    return {name: int(val) for name, val in re.findall(r"#define (APEX_ATTN_(?:OK|ERR_\w+))\s+(-?\d+)", text)}
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _lib.load()
+
+
+def test_library_exports_every_header_symbol(lib):
+    syms = header_symbols()
+    assert "apex_attn_fwd" in syms and len(syms) >= 6
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(syms) == set(_lib.SYMBOLS), "ctypes table out of sync with the header"
+
+
+def test_status_codes_match_header():
+    codes = header_codes()
+    for name, val in codes.items():
+        py = getattr(_lib, name.replace("APEX_ATTN_", ""))
+        assert py == val, name
+
+
+def test_strerror_covers_every_code(lib):
+    for name, val in header_codes().items():
+        msg = _lib.strerror(val)
+        assert msg and msg != "unknown status", name
+    assert _lib.strerror(12345) == "unknown status"
+
+
+def test_version_and_head_dims(lib):
+    assert lib.apex_attn_version() >= 100
+    for d in (64, 128):
+        assert lib.apex_attn_supports_head_dim(d) == 1
+    for d in (0, 32, 96, 512):
+        assert lib.apex_attn_supports_head_dim(d) == 0
+
+
+FAKE = 0x10000  # 16-byte aligned, never dereferenced: validation fails first
+
+
+def call(lib, q=FAKE, k=FAKE, v=FAKE, o=FAKE, lse=None, B=1, H=2, N=256, D=64, dtype=0,
+         causal=1, scale=0.125, strides=None):
+    if strides is None:
+        strides = [H * N * D, N * D, D] * 4
+    arr = (ctypes.c_longlong * 12)(*strides) if strides is not False else None
+    return lib.apex_attn_fwd(q, k, v, o, lse, B, H, N, D, dtype, causal, scale, arr, None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(o=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(strides=False), _lib.ERR_INVALID_ARGUMENT),
+    (dict(B=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(N=-5), _lib.ERR_INVALID_ARGUMENT),
+    (dict(D=96), _lib.ERR_UNSUPPORTED_HEAD_DIM),
+    (dict(D=32), _lib.ERR_UNSUPPORTED_HEAD_DIM),
+    (dict(dtype=2), _lib.ERR_UNSUPPORTED_DTYPE),
+    (dict(scale=0.0), _lib.ERR_BAD_SCALE),
+    (dict(scale=-1.0), _lib.ERR_BAD_SCALE),
+    (dict(scale=float("nan")), _lib.ERR_BAD_SCALE),
+    (dict(scale=float("inf")), _lib.ERR_BAD_SCALE),
+    (dict(strides=[2 * 256 * 64, 256 * 64, 60] * 4), _lib.ERR_BAD_LAYOUT),
+    (dict(strides=[2 * 256 * 64, 256 * 64, 32] * 4), _lib.ERR_BAD_LAYOUT),
+    (dict(strides=[2 * 256 * 64, -256 * 64, 64] * 4), _lib.ERR_BAD_LAYOUT),
+    (dict(q=FAKE + 8), _lib.ERR_BAD_LAYOUT),
+    (dict(lse=FAKE + 2), _lib.ERR_BAD_LAYOUT),
+    (dict(B=1 << 20, H=1 << 11), _lib.ERR_TOO_LARGE),
+])
+def test_argument_validation(lib, kw, code):
+    assert call(lib, **kw) == code
+
+
+def test_valid_arguments_without_device_report_no_device(lib):
+    # Host memory (or no GPU at all) is rejected after validation, never dereferenced.
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("checks the no-device path")
+    assert call(lib) == _lib.ERR_NO_DEVICE
