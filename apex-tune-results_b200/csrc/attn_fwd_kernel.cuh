@@ -57,7 +57,8 @@ static_assert(128 * (2 * kRegsSoftmax + kRegsEpilogue + kRegsOther) <= kThreads 
               "setmaxnreg split exceeds the launch register allocation");
 
 // Device status bits written by the kernel into the library's status word.
-constexpr int kStatusWaitTimeout = 1;
+constexpr int kStatusWaitTimeout = 1;   // a pipeline wait exceeded its limit
+constexpr int kStatusDrainTimeout = 2;  // an in-flight copy/MMA did not land at teardown
 
 struct AttnParams {
   void* o;
@@ -208,11 +209,17 @@ struct Waiter {
   }
 };
 
-// Wait used only while tearing down: ignores the abort flag, still bounded.
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
+// Wait used only while tearing down: ignores the abort flag, still bounded; a miss is
+// reported through the status word.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns,
+                                           int* status) {
+  if (ptx::mbar_try_wait(bar, parity)) return;
   const uint64_t t0 = ptx::globaltimer_ns();
   while (!ptx::mbar_try_wait(bar, parity)) {
-    if (ptx::globaltimer_ns() - t0 > limit_ns) return;
+    if (ptx::globaltimer_ns() - t0 > limit_ns) {
+      atomicOr(status, kStatusDrainTimeout);
+      return;
+    }
   }
 }
 
@@ -533,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // CTA releases TMEM and shared memory.
       if (lane == 0) {
         ptx::tc_commit(bar(Plan::kDrain));
-        drain_wait(bar(Plan::kDrain), 0, p.timeout_ns);
+        drain_wait(bar(Plan::kDrain), 0, p.timeout_ns, p.status);
       }
       __syncwarp();
     } else if (warp == 13) {
@@ -582,9 +589,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int last = fills < NS ? fills : NS;
         for (int k = 0; k < last; ++k) {
           const int f = fills - 1 - k;  // fill index
-          drain_wait(bar(Plan::kKvFull + (f % NS)), (uint32_t)((f / NS) & 1), p.timeout_ns);
+          drain_wait(bar(Plan::kKvFull + (f % NS)), (uint32_t)((f / NS) & 1), p.timeout_ns, p.status);
         }
-        if (q_filled) drain_wait(bar(Plan::kQFull), qe_par ^ 1, p.timeout_ns);
+        // qe_par equals the parity of the last Q fill's phase (it flips once per fill).
+        if (q_filled) drain_wait(bar(Plan::kQFull), qe_par, p.timeout_ns, p.status);
       }
       __syncwarp();
     }

@@ -300,6 +300,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["apex", "reference"], default="apex")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--only", choices=sorted(CONFIGS), default=None,
+                    help="run only the device-resident kernel leg of one config (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -335,6 +337,12 @@ def main():
     torch.cuda.set_device(device)
     import apex_attn
     peaks, peak_kind = load_peaks()
+    if args.only:
+        c = CONFIGS[args.only]
+        r = bench_config(args.only, c, args.steps, args.warmup, device)
+        print(json.dumps({"config": args.only, **c, **r, "frac_of_peak": r["tflops"] / peaks["bf16_tflops"],
+                          "device_status": apex_attn.device_status()}))
+        return
     c3 = CONFIGS["C3"]
     with ClockSampler(0) as clk:
         res = bench_config("C3", c3, args.steps, args.warmup, device)

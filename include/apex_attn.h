@@ -60,7 +60,8 @@ int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* l
 
 /*
  * Reads and clears the device status word of `device` after synchronising that
- * device. *flags receives the raw bits (1 = a kernel hit its bounded-wait limit).
+ * device. *flags receives the raw bits (1 = a kernel hit its bounded-wait limit,
+ * 2 = a copy or MMA still in flight at kernel teardown did not land within the limit).
  * Returns APEX_ATTN_ERR_DEVICE_TIMEOUT when any bit was set.
  * Has no counterpart in the reference (its Triton kernels cannot report device faults).
  */

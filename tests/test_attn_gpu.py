@@ -2,6 +2,9 @@
 
 Tolerances: output max-abs error <= 1e-2 against the fp32 math
 path on the same bf16/fp16 inputs; logsumexp (fp32 output) max-abs error <= 2e-3.
+Where outputs can exceed |o| = 4 (near one-hot softmax from large logits) a bf16 result
+cannot meet 1e-2 absolute: rounding to bf16 alone costs up to half an ulp, 2^-8 |o|.
+Those cases use |o - ref| <= 1e-2 + 2^-8 |ref| elementwise.
 """
 import math
 import os
@@ -45,7 +48,7 @@ def run(q, k, v, causal=True, sm_scale=None, lse=True):
     return out
 
 
-def check_vs_oracle(B, H, N, D, causal=True, dtype="bfloat16", seed=0, scale_q=1.0):
+def check_vs_oracle(B, H, N, D, causal=True, dtype="bfloat16", seed=0, scale_q=1.0, rel=0.0):
     q, k, v = make_inputs(B, H, N, D, seed=seed, dtype=dtype, scale_q=scale_q)
     o, lse = run(q.cuda(), k.cuda(), v.cuda(), causal=causal)
     ro, rl = attention_np(to_np32(q), to_np32(k), to_np32(v), causal=causal)
@@ -53,7 +56,8 @@ def check_vs_oracle(B, H, N, D, causal=True, dtype="bfloat16", seed=0, scale_q=1
     err = np.abs(o - ro).max()
     lerr = np.abs(lse.cpu().numpy() - rl).max()
     assert np.isfinite(o).all()
-    assert err <= O_TOL, f"max|o - oracle| = {err:.3e}"
+    excess = (np.abs(o - ro) - (O_TOL + rel * np.abs(ro))).max()
+    assert excess <= 0, f"max|o - oracle| = {err:.3e} (tolerance {O_TOL} + {rel}|ref|)"
     assert lerr <= LSE_TOL, f"max|lse - oracle| = {lerr:.3e}"
     return err
 
@@ -84,7 +88,7 @@ def test_fp16(D, causal):
 def test_large_logits_stay_finite(D):
     # q scaled x8: logits far beyond where the reference's rescale-free exp2 overflows
     # in fp16 (fused_attention.py:66,78); the rescaling softmax must stay exact.
-    check_vs_oracle(1, 2, 640, D, causal=True, seed=5, scale_q=8.0)
+    check_vs_oracle(1, 2, 640, D, causal=True, seed=5, scale_q=8.0, rel=2.0 ** -8)
 
 
 @pytest.mark.parametrize("path", cases(), ids=lambda p: os.path.basename(p)[:-4])
@@ -103,7 +107,8 @@ def test_golden_vectors(path):
         assert np.abs(o.float().cpu().numpy() - c["o_sdpa"]).max() < 5e-2
     else:
         ro, rl = c["o_sdpa"], c["lse_sdpa"]
-    assert np.abs(o.float().cpu().numpy() - ro).max() <= O_TOL
+    rel = 2.0 ** -8 if "bigq" in c["name"] else 0.0  # large-logit case: see module docstring
+    assert (np.abs(o.float().cpu().numpy() - ro) - (O_TOL + rel * np.abs(ro))).max() <= 0
     assert np.abs(lse.cpu().numpy() - rl).max() <= LSE_TOL
 
 
