@@ -42,6 +42,12 @@ SYMBOLS = {
          ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
          ctypes.c_float, _c_ll_p, ctypes.c_void_p],
     ),
+    "apex_attn_fwd_noalloc": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+         ctypes.c_float, _c_ll_p, ctypes.c_void_p],
+    ),
     "apex_attn_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "apex_attn_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p]),
     "apex_attn_strerror": (ctypes.c_char_p, [ctypes.c_int]),

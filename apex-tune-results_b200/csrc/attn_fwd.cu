@@ -300,3 +300,142 @@ int apex_attn_selftest_wait_timeout(int timeout_us, void* stream) {
 }
 
 }  // extern "C"
+
+// ============================================================================
+// Allocation-free variant: apex_attn_fwd_noalloc.
+//
+// Some callers cannot call cudaMalloc: code that runs while a memory pool or an
+// inference server owns the whole device budget, a plugin loaded into a host that
+// forbids allocations outside its own allocator, or a real-time loop in which an
+// allocation (and the device synchronisation it may imply) is not allowed. For them the
+// forward kernel's only scratch memory, the device status word that its bounded waits
+// write on a timeout, lives in the fixed array below instead of a cudaMalloc'd buffer.
+//
+// Every device that loads this library holds this array (256 bytes) until the process
+// exits. The forward kernel needs 4 bytes of it (one status word) whatever B, H, N and D
+// are, so no problem size needs more scratch than the array holds; requests outside the
+// kernel's supported range are rejected with APEX_ATTN_ERR_TOO_LARGE, as by apex_attn_fwd.
+//
+// In host code `g_noalloc_scratch` is only a host-side stand-in for the device array,
+// not a device address: a kernel given it would fault or use the wrong memory. The
+// device address is obtained once per device with cudaGetSymbolAddress, with that device
+// current, and passed to the kernel as a pointer.
+// ============================================================================
+namespace {
+
+constexpr int kNoAllocScratchBytes = 256;
+constexpr int kNoAllocStatusBytes = (int)sizeof(int);
+static_assert(kNoAllocStatusBytes <= kNoAllocScratchBytes, "status word must fit the static scratch");
+
+static __device__ __align__(256) int g_noalloc_scratch[kNoAllocScratchBytes / sizeof(int)];
+
+DeviceState g_noalloc_dev[kMaxDevices];  // status = device address of g_noalloc_scratch
+
+// Per-device set-up of the allocation-free path: device attributes, the tensor-map
+// encoder and the device address of the static scratch. Calls no allocating routine.
+int init_device_noalloc(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= kMaxDevices) return APEX_ATTN_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode_tried) {
+    g_encode_tried = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) ==
+            cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    else
+      (void)cudaGetLastError();
+  }
+  if (g_encode == nullptr) return APEX_ATTN_ERR_TENSOR_MAP;
+  DeviceState& s = g_noalloc_dev[dev];
+  if (!s.ready) {
+    if (cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&s.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&s.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_NO_DEVICE;
+    }
+    if (s.cc_major != 10 || s.cc_minor != 0) return APEX_ATTN_ERR_UNSUPPORTED_ARCH;
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_CUDA;
+    }
+    s.status = static_cast<int*>(ptr);
+    s.ready = true;
+  }
+  *out = &s;
+  return APEX_ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                                     int batch, int heads, int seqlen, int head_dim, int dtype,
+                                     int causal, float sm_scale, const long long* strides,
+                                     void* stream) {
+  // ---- argument validation (no CUDA calls), identical to apex_attn_fwd ----
+  if (!q || !k || !v || !o || !strides) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || heads <= 0 || seqlen <= 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (!apex_attn_supports_head_dim(head_dim)) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
+  if (dtype != APEX_ATTN_BF16 && dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
+  if (!std::isfinite(sm_scale) || !(sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
+  const long long BH = (long long)batch * heads;
+  const long long mblocks = (seqlen + apex::kItemRows - 1) / apex::kItemRows;
+  if (BH * mblocks > 0x7fffffffLL || seqlen > (1 << 30) || BH > (1LL << 30)) return APEX_ATTN_ERR_TOO_LARGE;
+  for (int i = 0; i < 12; ++i)
+    if (strides[i] < 0 || (strides[i] & 7) != 0 || strides[i] >= (1LL << 38)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  for (int t = 0; t < 4; ++t)
+    if (strides[3 * t + 2] < head_dim) return APEX_ATTN_ERR_BAD_LAYOUT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  if (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)) return APEX_ATTN_ERR_BAD_LAYOUT;
+
+  const int dev = device_of(q);
+  if (dev < 0 || device_of(k) != dev || device_of(v) != dev || device_of(o) != dev) return APEX_ATTN_ERR_NO_DEVICE;
+  if (lse && device_of(lse) != dev) return APEX_ATTN_ERR_NO_DEVICE;
+  DeviceGuard guard(dev);
+  DeviceState* ds = nullptr;
+  int rc = init_device_noalloc(dev, &ds);
+  if (rc != APEX_ATTN_OK) return rc;
+
+  CUtensorMap mq, mk, mv;
+  if ((rc = encode_map(&mq, q, dtype, batch, heads, seqlen, head_dim, strides[0], strides[1], strides[2])) ||
+      (rc = encode_map(&mk, k, dtype, batch, heads, seqlen, head_dim, strides[3], strides[4], strides[5])) ||
+      (rc = encode_map(&mv, v, dtype, batch, heads, seqlen, head_dim, strides[6], strides[7], strides[8])))
+    return rc;
+
+  AttnParams p{};
+  p.o = o;
+  p.lse = lse;
+  p.status = ds->status;
+  p.o_sb = strides[9];
+  p.o_sh = strides[10];
+  p.o_sn = strides[11];
+  p.B = batch;
+  p.H = heads;
+  p.N = seqlen;
+  p.num_mblocks = (int)mblocks;
+  p.num_kblocks = (seqlen + apex::kBlockN - 1) / apex::kBlockN;
+  p.num_items = (int)(BH * mblocks);
+  const double kv_bytes_per_head = 2.0 * seqlen * head_dim * 2.0;
+  long long g = (long long)(48.0 * 1024 * 1024 / kv_bytes_per_head);
+  p.group_heads = (int)std::max(1LL, std::min(g, BH));
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.causal = causal ? 1 : 0;
+  p.timeout_ns = wait_timeout_ns();
+  const int grid = std::min(p.num_items, ds->num_sms);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  // The scratch keeps the previous call's contents: the status word must start at zero.
+  if (cudaMemsetAsync(ds->status, 0, kNoAllocStatusBytes, s) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_CUDA;
+  }
+  if (head_dim == 64) {
+    if (dtype == APEX_ATTN_BF16) return launch<64, __nv_bfloat16, 8>(*ds, 1u, mq, mk, mv, p, grid, s);
+    return launch<64, __half, 8>(*ds, 2u, mq, mk, mv, p, grid, s);
+  }
+  if (dtype == APEX_ATTN_BF16) return launch<128, __nv_bfloat16, 4>(*ds, 4u, mq, mk, mv, p, grid, s);
+  return launch<128, __half, 4>(*ds, 8u, mq, mk, mv, p, grid, s);
+}

@@ -75,6 +75,31 @@ int apex_attn_device_status(int device, int* flags);
  */
 int apex_attn_selftest_wait_timeout(int timeout_us, void* stream);
 
+/*
+ * Allocation-free form of apex_attn_fwd: same arguments, same kernel, same results.
+ * No counterpart in the reference; it exists for callers that cannot call cudaMalloc
+ * (a process whose device memory is owned by a pool or a serving runtime, a plugin in a
+ * host that forbids allocations outside its own allocator, a real-time loop).
+ *
+ * The caller passes the inputs and outputs as for apex_attn_fwd. The kernel's scratch
+ * (its 4-byte device status word) lives in a fixed 256-byte static device array of the
+ * library that every device loading the library holds until process exit; this entry
+ * point calls no cudaMalloc, cudaFree or other allocating routine. The scratch need does
+ * not grow with B, H, N or D; sizes outside the kernel's supported range are rejected
+ * with APEX_ATTN_ERR_TOO_LARGE.
+ *
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * and sets kernel attributes for that device, so make it before any stream capture.
+ * Each call clears the status word on `stream` before its kernel. All calls share the
+ * array: calls that overlap on the GPU (other streams, other threads) race on it. A
+ * bounded wait that expires still ends the kernel early, but its status bit stays in the
+ * shared scratch, which apex_attn_device_status does not read; callers that need
+ * device-fault reports use apex_attn_fwd.
+ */
+int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                          int batch, int heads, int seqlen, int head_dim, int dtype, int causal,
+                          float sm_scale, const long long* strides, void* stream);
+
 /* Human-readable text for a status code. Replaces the exception text the reference
  * harness prints on failure (submission.py:299-306). */
 const char* apex_attn_strerror(int status);
