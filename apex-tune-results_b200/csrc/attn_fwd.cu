@@ -7,7 +7,7 @@
 // descriptors for d=128 (:165-169) and launch a grid of (ceil(N/128), B*H) programs.
 // Here the caller owns every buffer; this file validates the layout, encodes 4-D TMA
 // tensor maps (so strided [B,H,N,D] and [B,N,H,D] views need no copy), and launches one
-// persistent CTA per SM.
+// persistent CTA per SM with the per-head-dim configuration apex::Cfg<D>.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -25,7 +25,22 @@ namespace {
 
 using apex::AttnParams;
 
-constexpr int kVersion = 100;  // 0.1.0
+constexpr int kVersion = 200;  // 0.2.0
+
+// Build-time tuning knob (overridable with -D for sweeps): exp2 pairs out of every 8 of an
+// unmasked tile that use the FMA-pipe polynomial, per head dim.
+#ifndef APEX_EMU64
+#define APEX_EMU64 0
+#endif
+#ifndef APEX_EMU128
+#define APEX_EMU128 0
+#endif
+#ifndef APEX_EMU256
+#define APEX_EMU256 0
+#endif
+template <int D>
+constexpr int kEmu = D == 64 ? APEX_EMU64 : (D == 128 ? APEX_EMU128 : APEX_EMU256);
+
 constexpr int kMaxDevices = 64;
 constexpr int kStatusBytes = 256;
 
@@ -52,9 +67,8 @@ unsigned long long wait_timeout_ns() {
   return v;
 }
 
-int init_device(int dev, DeviceState** out) {
-  if (dev < 0 || dev >= kMaxDevices) return APEX_ATTN_ERR_NO_DEVICE;
-  std::lock_guard<std::mutex> lk(g_mu);
+// Resolves cuTensorMapEncodeTiled once (caller holds g_mu).
+bool resolve_encode_locked() {
   if (!g_encode_tried) {
     g_encode_tried = true;
     void* fn = nullptr;
@@ -66,16 +80,29 @@ int init_device(int dev, DeviceState** out) {
     else
       (void)cudaGetLastError();
   }
-  if (g_encode == nullptr) return APEX_ATTN_ERR_TENSOR_MAP;
+  return g_encode != nullptr;
+}
+
+// Device attributes shared by both state kinds (caller holds g_mu).
+int probe_device_locked(int dev, DeviceState& s) {
+  if (cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&s.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&s.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_NO_DEVICE;
+  }
+  if (s.cc_major != 10 || s.cc_minor != 0) return APEX_ATTN_ERR_UNSUPPORTED_ARCH;
+  return APEX_ATTN_OK;
+}
+
+int init_device(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= kMaxDevices) return APEX_ATTN_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!resolve_encode_locked()) return APEX_ATTN_ERR_TENSOR_MAP;
   DeviceState& s = g_dev[dev];
   if (!s.ready) {
-    if (cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&s.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&s.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return APEX_ATTN_ERR_NO_DEVICE;
-    }
-    if (s.cc_major != 10 || s.cc_minor != 0) return APEX_ATTN_ERR_UNSUPPORTED_ARCH;
+    int rc = probe_device_locked(dev, s);
+    if (rc != APEX_ATTN_OK) return rc;
     if (cudaMalloc(&s.status, kStatusBytes) != cudaSuccess) {
       (void)cudaGetLastError();
       return APEX_ATTN_ERR_CUDA;
@@ -89,6 +116,58 @@ int init_device(int dev, DeviceState** out) {
   *out = &s;
   return APEX_ATTN_OK;
 }
+
+// ----------------------------------------------------------------------------
+// Allocation-free state (apex_attn_fwd_noalloc).
+//
+// Some callers cannot call cudaMalloc: code that runs while a memory pool or an
+// inference server owns the whole device budget, a plugin loaded into a host that
+// forbids allocations outside its own allocator, or a real-time loop in which an
+// allocation (and the device synchronisation it may imply) is not allowed. For them the
+// forward kernel's only scratch memory, the device status word that its bounded waits
+// write on a timeout, lives in the fixed array below instead of a cudaMalloc'd buffer.
+//
+// Every device that loads this library holds this array (256 bytes) until the process
+// exits. The forward kernel needs 4 bytes of it (one status word) whatever B, H, N and D
+// are, so no problem size needs more scratch than the array holds; requests outside the
+// kernel's supported range are rejected with APEX_ATTN_ERR_TOO_LARGE, as by apex_attn_fwd.
+//
+// In host code `g_noalloc_scratch` is only a host-side stand-in for the device array,
+// not a device address: a kernel given it would fault or use the wrong memory. The
+// device address is obtained once per device with cudaGetSymbolAddress, with that device
+// current, and passed to the kernel as a pointer.
+// ----------------------------------------------------------------------------
+constexpr int kNoAllocScratchBytes = 256;
+constexpr int kNoAllocStatusBytes = (int)sizeof(int);
+static_assert(kNoAllocStatusBytes <= kNoAllocScratchBytes, "status word must fit the static scratch");
+
+static __device__ __align__(256) int g_noalloc_scratch[kNoAllocScratchBytes / sizeof(int)];
+
+DeviceState g_noalloc_dev[kMaxDevices];  // status = device address of g_noalloc_scratch
+
+// Per-device set-up of the allocation-free path: device attributes, the tensor-map
+// encoder and the device address of the static scratch. Calls no allocating routine.
+int init_device_noalloc(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= kMaxDevices) return APEX_ATTN_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!resolve_encode_locked()) return APEX_ATTN_ERR_TENSOR_MAP;
+  DeviceState& s = g_noalloc_dev[dev];
+  if (!s.ready) {
+    int rc = probe_device_locked(dev, s);
+    if (rc != APEX_ATTN_OK) return rc;
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_CUDA;
+    }
+    s.status = static_cast<int*>(ptr);
+    s.ready = true;
+  }
+  *out = &s;
+  return APEX_ATTN_OK;
+}
+
+// ----------------------------------------------------------------------------
 
 // Resolves the device that owns `ptr`; -1 when it is not device memory.
 int device_of(const void* ptr) {
@@ -119,11 +198,11 @@ int encode_map(CUtensorMap* m, const void* ptr, int dtype, int B, int H, int N, 
   return r == CUDA_SUCCESS ? APEX_ATTN_OK : APEX_ATTN_ERR_TENSOR_MAP;
 }
 
-template <int D, typename T, int NS>
+template <int D, typename T>
 int launch(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
            const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
-  auto kern = apex::attn_fwd_sm100_kernel<D, T, NS>;
-  constexpr int smem = apex::SmemPlan<D, NS>::kDynamicBytes;
+  auto kern = apex::attn_fwd_sm100_kernel<D, T, kEmu<D>>;
+  constexpr int smem = apex::SmemPlan<D>::kDynamicBytes;
   if (!(ds.attr_done & attr_bit)) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
@@ -132,12 +211,20 @@ int launch(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUte
     }
     ds.attr_done |= attr_bit;
   }
-  kern<<<grid, apex::kThreads, smem, stream>>>(mq, mk, mv, p);
+  kern<<<grid, apex::Cfg<D>::kThreads, smem, stream>>>(mq, mk, mv, p);
   if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
   return APEX_ATTN_OK;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int item_rows(int head_dim) {
+  switch (head_dim) {
+    case 64: return apex::Cfg<64>::kItemRows;
+    case 128: return apex::Cfg<128>::kItemRows;
+    default: return apex::Cfg<256>::kItemRows;
+  }
+}
 
 struct DeviceGuard {
   int prev = -1;
@@ -170,44 +257,22 @@ __global__ void wait_timeout_selftest_kernel(int* status, unsigned long long tim
   __syncthreads();
 }
 
-}  // namespace
+bool supported_head_dim(int head_dim) { return head_dim == 64 || head_dim == 128 || head_dim == 256; }
 
-extern "C" {
-
-int apex_attn_version(void) { return kVersion; }
-
-int apex_attn_supports_head_dim(int head_dim) { return (head_dim == 64 || head_dim == 128) ? 1 : 0; }
-
-const char* apex_attn_strerror(int status) {
-  switch (status) {
-    case APEX_ATTN_OK: return "success";
-    case APEX_ATTN_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer or non-positive size)";
-    case APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM: return "unsupported head dim (supported: 64, 128)";
-    case APEX_ATTN_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (supported: bf16, fp16)";
-    case APEX_ATTN_ERR_BAD_LAYOUT: return "layout not supported: head-dim stride must be 1, other strides multiples of 8 elements, pointers 16-byte aligned";
-    case APEX_ATTN_ERR_BAD_SCALE: return "sm_scale must be finite and > 0";
-    case APEX_ATTN_ERR_NO_DEVICE: return "tensors are not CUDA device memory on one device";
-    case APEX_ATTN_ERR_UNSUPPORTED_ARCH: return "device is not sm_100 (B200)";
-    case APEX_ATTN_ERR_TENSOR_MAP: return "TMA tensor map encoding failed";
-    case APEX_ATTN_ERR_LAUNCH: return "kernel launch failed";
-    case APEX_ATTN_ERR_DEVICE_TIMEOUT: return "a kernel hit its bounded-wait limit (device status set)";
-    case APEX_ATTN_ERR_TOO_LARGE: return "sizes exceed the supported range";
-    case APEX_ATTN_ERR_CUDA: return "CUDA runtime error";
-    default: return "unknown status";
-  }
-}
-
-int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
-                  int heads, int seqlen, int head_dim, int dtype, int causal, float sm_scale,
-                  const long long* strides, void* stream) {
+// Validation, tensor maps, parameters and dispatch shared by both forward entry points.
+// `noalloc` selects the allocation-free device state and clears its status word first.
+int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, float* lse, int batch,
+            int heads, int seqlen, int head_dim, int dtype, int causal, float sm_scale,
+            const long long* strides, void* stream) {
   // ---- argument validation (no CUDA calls) ----
   if (!q || !k || !v || !o || !strides) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   if (batch <= 0 || heads <= 0 || seqlen <= 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
-  if (!apex_attn_supports_head_dim(head_dim)) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
+  if (!supported_head_dim(head_dim)) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
   if (dtype != APEX_ATTN_BF16 && dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
   if (!std::isfinite(sm_scale) || !(sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
   const long long BH = (long long)batch * heads;
-  const long long mblocks = (seqlen + apex::kItemRows - 1) / apex::kItemRows;
+  const int rows_per_item = item_rows(head_dim);
+  const long long mblocks = (seqlen + rows_per_item - 1) / rows_per_item;
   if (BH * mblocks > 0x7fffffffLL || seqlen > (1 << 30) || BH > (1LL << 30)) return APEX_ATTN_ERR_TOO_LARGE;
   for (int i = 0; i < 12; ++i)
     if (strides[i] < 0 || (strides[i] & 7) != 0 || strides[i] >= (1LL << 38)) return APEX_ATTN_ERR_BAD_LAYOUT;
@@ -222,7 +287,7 @@ int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* l
   if (lse && device_of(lse) != dev) return APEX_ATTN_ERR_NO_DEVICE;
   DeviceGuard guard(dev);
   DeviceState* ds = nullptr;
-  int rc = init_device(dev, &ds);
+  int rc = noalloc ? init_device_noalloc(dev, &ds) : init_device(dev, &ds);
   if (rc != APEX_ATTN_OK) return rc;
 
   CUtensorMap mq, mk, mv;
@@ -255,12 +320,67 @@ int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* l
   const int grid = std::min(p.num_items, ds->num_sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
-  if (head_dim == 64) {
-    if (dtype == APEX_ATTN_BF16) return launch<64, __nv_bfloat16, 8>(*ds, 1u, mq, mk, mv, p, grid, s);
-    return launch<64, __half, 8>(*ds, 2u, mq, mk, mv, p, grid, s);
+  if (noalloc) {
+    // The static scratch keeps the previous call's contents: the status word must start
+    // at zero.
+    if (cudaMemsetAsync(ds->status, 0, kNoAllocStatusBytes, s) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_CUDA;
+    }
   }
-  if (dtype == APEX_ATTN_BF16) return launch<128, __nv_bfloat16, 4>(*ds, 4u, mq, mk, mv, p, grid, s);
-  return launch<128, __half, 4>(*ds, 8u, mq, mk, mv, p, grid, s);
+  const bool bf16 = dtype == APEX_ATTN_BF16;
+  switch (head_dim) {
+    case 64:
+      return bf16 ? launch<64, __nv_bfloat16>(*ds, 1u, mq, mk, mv, p, grid, s)
+                  : launch<64, __half>(*ds, 2u, mq, mk, mv, p, grid, s);
+    case 128:
+      return bf16 ? launch<128, __nv_bfloat16>(*ds, 4u, mq, mk, mv, p, grid, s)
+                  : launch<128, __half>(*ds, 8u, mq, mk, mv, p, grid, s);
+    default:
+      return bf16 ? launch<256, __nv_bfloat16>(*ds, 16u, mq, mk, mv, p, grid, s)
+                  : launch<256, __half>(*ds, 32u, mq, mk, mv, p, grid, s);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int apex_attn_version(void) { return kVersion; }
+
+int apex_attn_supports_head_dim(int head_dim) { return supported_head_dim(head_dim) ? 1 : 0; }
+
+const char* apex_attn_strerror(int status) {
+  switch (status) {
+    case APEX_ATTN_OK: return "success";
+    case APEX_ATTN_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer or non-positive size)";
+    case APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM: return "unsupported head dim (supported: 64, 128, 256)";
+    case APEX_ATTN_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (supported: bf16, fp16)";
+    case APEX_ATTN_ERR_BAD_LAYOUT: return "layout not supported: head-dim stride must be 1, other strides multiples of 8 elements, pointers 16-byte aligned";
+    case APEX_ATTN_ERR_BAD_SCALE: return "sm_scale must be finite and > 0";
+    case APEX_ATTN_ERR_NO_DEVICE: return "tensors are not CUDA device memory on one device";
+    case APEX_ATTN_ERR_UNSUPPORTED_ARCH: return "device is not sm_100 (B200)";
+    case APEX_ATTN_ERR_TENSOR_MAP: return "TMA tensor map encoding failed";
+    case APEX_ATTN_ERR_LAUNCH: return "kernel launch failed";
+    case APEX_ATTN_ERR_DEVICE_TIMEOUT: return "a kernel reported a device-side error (bounded-wait limit or shared-memory alignment; device status set)";
+    case APEX_ATTN_ERR_TOO_LARGE: return "sizes exceed the supported range";
+    case APEX_ATTN_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
+                  int heads, int seqlen, int head_dim, int dtype, int causal, float sm_scale,
+                  const long long* strides, void* stream) {
+  return forward(false, q, k, v, o, lse, batch, heads, seqlen, head_dim, dtype, causal, sm_scale,
+                 strides, stream);
+}
+
+int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                          int batch, int heads, int seqlen, int head_dim, int dtype, int causal,
+                          float sm_scale, const long long* strides, void* stream) {
+  return forward(true, q, k, v, o, lse, batch, heads, seqlen, head_dim, dtype, causal, sm_scale,
+                 strides, stream);
 }
 
 int apex_attn_device_status(int device, int* flags) {
@@ -300,142 +420,3 @@ int apex_attn_selftest_wait_timeout(int timeout_us, void* stream) {
 }
 
 }  // extern "C"
-
-// ============================================================================
-// Allocation-free variant: apex_attn_fwd_noalloc.
-//
-// Some callers cannot call cudaMalloc: code that runs while a memory pool or an
-// inference server owns the whole device budget, a plugin loaded into a host that
-// forbids allocations outside its own allocator, or a real-time loop in which an
-// allocation (and the device synchronisation it may imply) is not allowed. For them the
-// forward kernel's only scratch memory, the device status word that its bounded waits
-// write on a timeout, lives in the fixed array below instead of a cudaMalloc'd buffer.
-//
-// Every device that loads this library holds this array (256 bytes) until the process
-// exits. The forward kernel needs 4 bytes of it (one status word) whatever B, H, N and D
-// are, so no problem size needs more scratch than the array holds; requests outside the
-// kernel's supported range are rejected with APEX_ATTN_ERR_TOO_LARGE, as by apex_attn_fwd.
-//
-// In host code `g_noalloc_scratch` is only a host-side stand-in for the device array,
-// not a device address: a kernel given it would fault or use the wrong memory. The
-// device address is obtained once per device with cudaGetSymbolAddress, with that device
-// current, and passed to the kernel as a pointer.
-// ============================================================================
-namespace {
-
-constexpr int kNoAllocScratchBytes = 256;
-constexpr int kNoAllocStatusBytes = (int)sizeof(int);
-static_assert(kNoAllocStatusBytes <= kNoAllocScratchBytes, "status word must fit the static scratch");
-
-static __device__ __align__(256) int g_noalloc_scratch[kNoAllocScratchBytes / sizeof(int)];
-
-DeviceState g_noalloc_dev[kMaxDevices];  // status = device address of g_noalloc_scratch
-
-// Per-device set-up of the allocation-free path: device attributes, the tensor-map
-// encoder and the device address of the static scratch. Calls no allocating routine.
-int init_device_noalloc(int dev, DeviceState** out) {
-  if (dev < 0 || dev >= kMaxDevices) return APEX_ATTN_ERR_NO_DEVICE;
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_encode_tried) {
-    g_encode_tried = true;
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult qres;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres) ==
-            cudaSuccess &&
-        qres == cudaDriverEntryPointSuccess)
-      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    else
-      (void)cudaGetLastError();
-  }
-  if (g_encode == nullptr) return APEX_ATTN_ERR_TENSOR_MAP;
-  DeviceState& s = g_noalloc_dev[dev];
-  if (!s.ready) {
-    if (cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&s.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&s.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return APEX_ATTN_ERR_NO_DEVICE;
-    }
-    if (s.cc_major != 10 || s.cc_minor != 0) return APEX_ATTN_ERR_UNSUPPORTED_ARCH;
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
-      (void)cudaGetLastError();
-      return APEX_ATTN_ERR_CUDA;
-    }
-    s.status = static_cast<int*>(ptr);
-    s.ready = true;
-  }
-  *out = &s;
-  return APEX_ATTN_OK;
-}
-
-}  // namespace
-
-extern "C" int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
-                                     int batch, int heads, int seqlen, int head_dim, int dtype,
-                                     int causal, float sm_scale, const long long* strides,
-                                     void* stream) {
-  // ---- argument validation (no CUDA calls), identical to apex_attn_fwd ----
-  if (!q || !k || !v || !o || !strides) return APEX_ATTN_ERR_INVALID_ARGUMENT;
-  if (batch <= 0 || heads <= 0 || seqlen <= 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
-  if (!apex_attn_supports_head_dim(head_dim)) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
-  if (dtype != APEX_ATTN_BF16 && dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
-  if (!std::isfinite(sm_scale) || !(sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
-  const long long BH = (long long)batch * heads;
-  const long long mblocks = (seqlen + apex::kItemRows - 1) / apex::kItemRows;
-  if (BH * mblocks > 0x7fffffffLL || seqlen > (1 << 30) || BH > (1LL << 30)) return APEX_ATTN_ERR_TOO_LARGE;
-  for (int i = 0; i < 12; ++i)
-    if (strides[i] < 0 || (strides[i] & 7) != 0 || strides[i] >= (1LL << 38)) return APEX_ATTN_ERR_BAD_LAYOUT;
-  for (int t = 0; t < 4; ++t)
-    if (strides[3 * t + 2] < head_dim) return APEX_ATTN_ERR_BAD_LAYOUT;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return APEX_ATTN_ERR_BAD_LAYOUT;
-  if (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)) return APEX_ATTN_ERR_BAD_LAYOUT;
-
-  const int dev = device_of(q);
-  if (dev < 0 || device_of(k) != dev || device_of(v) != dev || device_of(o) != dev) return APEX_ATTN_ERR_NO_DEVICE;
-  if (lse && device_of(lse) != dev) return APEX_ATTN_ERR_NO_DEVICE;
-  DeviceGuard guard(dev);
-  DeviceState* ds = nullptr;
-  int rc = init_device_noalloc(dev, &ds);
-  if (rc != APEX_ATTN_OK) return rc;
-
-  CUtensorMap mq, mk, mv;
-  if ((rc = encode_map(&mq, q, dtype, batch, heads, seqlen, head_dim, strides[0], strides[1], strides[2])) ||
-      (rc = encode_map(&mk, k, dtype, batch, heads, seqlen, head_dim, strides[3], strides[4], strides[5])) ||
-      (rc = encode_map(&mv, v, dtype, batch, heads, seqlen, head_dim, strides[6], strides[7], strides[8])))
-    return rc;
-
-  AttnParams p{};
-  p.o = o;
-  p.lse = lse;
-  p.status = ds->status;
-  p.o_sb = strides[9];
-  p.o_sh = strides[10];
-  p.o_sn = strides[11];
-  p.B = batch;
-  p.H = heads;
-  p.N = seqlen;
-  p.num_mblocks = (int)mblocks;
-  p.num_kblocks = (seqlen + apex::kBlockN - 1) / apex::kBlockN;
-  p.num_items = (int)(BH * mblocks);
-  const double kv_bytes_per_head = 2.0 * seqlen * head_dim * 2.0;
-  long long g = (long long)(48.0 * 1024 * 1024 / kv_bytes_per_head);
-  p.group_heads = (int)std::max(1LL, std::min(g, BH));
-  p.scale_log2 = sm_scale * 1.4426950408889634f;
-  p.causal = causal ? 1 : 0;
-  p.timeout_ns = wait_timeout_ns();
-  const int grid = std::min(p.num_items, ds->num_sms);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-
-  // The scratch keeps the previous call's contents: the status word must start at zero.
-  if (cudaMemsetAsync(ds->status, 0, kNoAllocStatusBytes, s) != cudaSuccess) {
-    (void)cudaGetLastError();
-    return APEX_ATTN_ERR_CUDA;
-  }
-  if (head_dim == 64) {
-    if (dtype == APEX_ATTN_BF16) return launch<64, __nv_bfloat16, 8>(*ds, 1u, mq, mk, mv, p, grid, s);
-    return launch<64, __half, 8>(*ds, 2u, mq, mk, mv, p, grid, s);
-  }
-  if (dtype == APEX_ATTN_BF16) return launch<128, __nv_bfloat16, 4>(*ds, 4u, mq, mk, mv, p, grid, s);
-  return launch<128, __half, 4>(*ds, 8u, mq, mk, mv, p, grid, s);
-}

@@ -5,29 +5,29 @@
 // with an optional causal mask, fp32 accumulation, output in the input dtype), re-designed
 // for Blackwell rather than translated:
 //
-//   * one CTA per SM, looping over work items (b, h, 256-row query block) in a
-//     longest-first order grouped by heads so that concurrently running CTAs share K/V in L2
-//     (the reference only reverses the m-block order, fused_attention.py:33-36);
-//   * warp roles (16 warps):
-//       warps 0-3   softmax for query sub-tile 0 (rows m0 .. m0+127)
-//       warps 4-7   softmax for query sub-tile 1 (rows m0+128 .. m0+255)
-//       warps 8-11  epilogue: O * (1/l) -> bf16/fp16 -> global, and the fp32 logsumexp
-//       warp 12     tcgen05.mma issuer (one thread) + TMEM allocation
-//       warp 13     TMA producer (one thread): Q once per item, K/V through an NS-stage ring
-//       warps 14-15 idle
-//   * S = Q K^T and O += P V run on the 5th-generation tensor cores with both
-//     accumulators in TMEM; P is written back into S's TMEM columns and fed to the
-//     second GEMM straight from TMEM;
-//   * the online softmax keeps a stale running max and rescales O only when the
-//     row max grows by more than kRescaleLog2 (log2 units). That keeps most of the
-//     reference's "rescale-free" speed (fused_attention.py:61-82) without its
-//     overflow hazard for large logits.
+//   * one CTA per SM, looping over work items (b, h, query block of kSub x 128 rows) in a
+//     longest-first order grouped by heads so that concurrently running CTAs share K/V in
+//     L2 (the reference only reverses the m-block order, fused_attention.py:33-36);
+//   * S = Q K^T and O += P V run on the 5th-generation tensor cores (tcgen05.mma) with both
+//     accumulators in TMEM;
+//   * P never aliases S: it has its own buffer (TMEM columns for d = 64 and 256, shared
+//     memory for d = 128, where S and O fill all 512 TMEM columns). So the next S of a
+//     query sub-tile is issued as soon as its softmax warps have read the current S into
+//     registers, and the softmax warps run back to back instead of waiting for P.V and
+//     the next S after every tile;
+//   * one MMA-issuing warp per query sub-tile, each walking the shared K/V ring;
+//   * the online softmax keeps a stale running max and rescales O only when a row max
+//     grows by more than kRescaleLog2 (log2 units). That keeps most of the reference's
+//     "rescale-free" speed (fused_attention.py:61-82) without its overflow hazard for large
+//     logits.
 //
-// TMEM map (512 columns x 128 lanes, lane = query row of a sub-tile):
-//   [0,128)   S0 / P0 (P0 packed 2 x 16-bit per column in [0,64))
-//   [128,256) S1 / P1
-//   [256,256+D)     O0
-//   [256+D,256+2D)  O1
+// Warp roles (kSub = 2: d = 64, 128; kSub = 1: d = 256):
+//   warps [0, 4 kSub)           softmax, one warpgroup per query sub-tile (thread = row)
+//   next 4 warps                epilogue: O * (1/l) -> bf16/fp16 -> global, fp32 logsumexp
+//   next kSub warps             tcgen05.mma issuers (warp of sub-tile i; the first also
+//                               allocates TMEM)
+//   next kSub warps             TMA producers: Q of sub-tile i; the first also fills the
+//                               K/V ring
 #pragma once
 
 #include <cuda.h>
@@ -36,6 +36,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "sm100_ptx.cuh"
 
@@ -43,22 +44,12 @@ namespace apex {
 
 constexpr int kBlockM = 128;   // query rows per sub-tile (= TMEM lanes)
 constexpr int kBlockN = 128;   // keys per K/V tile
-constexpr int kItemRows = 2 * kBlockM;
-constexpr int kThreads = 512;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the max grows by > 2^8
-
-// Per-thread register budgets after setmaxnreg. setmaxnreg.inc draws on the registers the
-// block was launched with (512 threads x 128, from __launch_bounds__(512, 1)); a split whose
-// sum exceeds that would block forever, so it is checked at compile time.
-constexpr int kRegsSoftmax = 184;   // 2 warpgroups
-constexpr int kRegsEpilogue = 80;   // 1 warpgroup
-constexpr int kRegsOther = 56;      // MMA, producer, 2 idle warps
-static_assert(128 * (2 * kRegsSoftmax + kRegsEpilogue + kRegsOther) <= kThreads * 128,
-              "setmaxnreg split exceeds the launch register allocation");
 
 // Device status bits written by the kernel into the library's status word.
 constexpr int kStatusWaitTimeout = 1;   // a pipeline wait exceeded its limit
 constexpr int kStatusDrainTimeout = 2;  // an in-flight copy/MMA did not land at teardown
+constexpr int kStatusSmemAlign = 4;     // dynamic shared memory not 1 KB aligned (not run)
 
 struct AttnParams {
   void* o;
@@ -66,13 +57,41 @@ struct AttnParams {
   int* status;       // device status word (bitmask of kStatus*)
   long long o_sb, o_sh, o_sn;  // output strides in elements (d stride is 1)
   int B, H, N;
-  int num_mblocks;   // ceil(N / 256)
+  int num_mblocks;   // ceil(N / item rows)
   int num_kblocks;   // ceil(N / 128)
   int num_items;     // B * H * num_mblocks
   int group_heads;   // heads per L2 scheduling group
   float scale_log2;  // sm_scale * log2(e)
   int causal;
   unsigned long long timeout_ns;
+};
+
+// Per-head-dim configuration (replaces _CONFIGS, fused_attention.py:148-152).
+template <int D>
+struct Cfg {
+  static_assert(D == 64 || D == 128 || D == 256, "head dims 64, 128, 256");
+  static constexpr int kSub = D == 256 ? 1 : 2;          // 128-row query sub-tiles per item
+  static constexpr bool kPInTmem = D != 128;             // else P lives in shared memory
+  static constexpr int kParts = D == 256 ? 2 : 1;        // ring stages per K or V tile
+  static constexpr int kStageCols = D / kParts;          // head-dim columns per stage
+  static constexpr int kNS = D == 64 ? 8 : (D == 128 ? 3 : 5);  // ring stages
+  static constexpr int kThreads = 128 * (kSub + 2);
+  static constexpr int kItemRows = kSub * kBlockM;
+  // TMEM columns: S_i at i*128; O_i at kTmemO + i*D; P_i at kTmemP + i*64 (TMEM variants).
+  static constexpr int kTmemO = 256;
+  static constexpr int kTmemP = D == 64 ? 384 : 128;
+  // setmaxnreg budgets (multiples of 8): softmax, epilogue, the remaining warpgroup. Their
+  // sum x 128 must not exceed the launch allocation (kThreads x (65536 / kThreads)), or
+  // setmaxnreg.inc would wait forever; checked below.
+  static constexpr int kRegsSoftmax = kSub == 2 ? 184 : 240;
+  static constexpr int kRegsEpilogue = kSub == 2 ? 80 : 128;
+  static constexpr int kRegsOther = kSub == 2 ? 56 : 136;
+  static constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
+  static_assert(128 * (kSub * kRegsSoftmax + kRegsEpilogue + kRegsOther) <= kThreads * kLaunchRegs,
+                "setmaxnreg split exceeds the launch register allocation");
+  static_assert(kTmemO + kSub * D <= 512, "TMEM plan overflows 512 columns");
+  static_assert(!kPInTmem || kTmemP + kSub * 64 <= kTmemO || kTmemP >= kTmemO + kSub * D,
+                "P columns overlap O");
 };
 
 template <typename T>
@@ -112,41 +131,56 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr, uint32_t lb
          ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// Shared-memory plan. A 128-row tile of D columns is stored as D/64 column chunks,
-// each 128 rows x 128 bytes with the TMA 128B swizzle (16 KB per chunk).
-template <int D, int NS>
+// Shared-memory plan. A 128-row tile of C columns is stored as C/64 column chunks, each
+// 128 rows x 128 bytes with the 128-byte swizzle (16 KB per chunk): the layout the TMA
+// writes and tcgen05.mma reads for K-major operands. The 1 KB-aligned tile region comes
+// first; barriers and row statistics follow it.
+template <int D>
 struct SmemPlan {
+  using C = Cfg<D>;
   static constexpr int kChunkBytes = kBlockM * 128;
-  static constexpr int kTileBytes = kBlockM * D * 2;
+  static constexpr int kQTileBytes = kBlockM * D * 2;                 // one sub-tile
+  static constexpr int kStageBytes = kBlockN * C::kStageCols * 2;
+  static constexpr int kPTileBytes = kBlockM * kBlockN * 2;           // one sub-tile
   static constexpr int kQ = 0;
-  static constexpr int kKV = kQ + 2 * kTileBytes;
-  static constexpr int kBars = kKV + NS * kTileBytes;
+  static constexpr int kP = kQ + C::kSub * kQTileBytes;
+  static constexpr int kKV = kP + (C::kPInTmem ? 0 : C::kSub * kPTileBytes);
+  static constexpr int kBars = kKV + C::kNS * kStageBytes;
   // barrier slots
+  static constexpr int NS = C::kNS, S = C::kSub;
   static constexpr int kKvFull = 0;
   static constexpr int kKvEmpty = NS;
   static constexpr int kQFull = 2 * NS;
-  static constexpr int kQEmpty = 2 * NS + 1;
-  static constexpr int kSFull = 2 * NS + 2;    // [2]
-  static constexpr int kPFull = 2 * NS + 4;    // [2]
-  static constexpr int kOFull = 2 * NS + 6;    // [2]
-  static constexpr int kOEmpty = 2 * NS + 8;   // [2]
-  static constexpr int kLFull = 2 * NS + 10;   // [2]
-  static constexpr int kLEmpty = 2 * NS + 12;  // [2]
-  static constexpr int kDrain = 2 * NS + 14;
-  static constexpr int kNumBars = 2 * NS + 15;
-  static constexpr int kRowStats = (kBars + kNumBars * 8 + 15) / 16 * 16;  // float l[2][128], m[2][128]
-  static constexpr int kMisc = kRowStats + 4 * kBlockM * 4;                // tmem base, abort flag
+  static constexpr int kQEmpty = kQFull + S;
+  static constexpr int kSFull = kQEmpty + S;
+  static constexpr int kSFree = kSFull + S;
+  static constexpr int kPFull = kSFree + S;
+  static constexpr int kPFree = kPFull + S;
+  static constexpr int kOFull = kPFree + S;
+  static constexpr int kOEmpty = kOFull + S;
+  static constexpr int kLFull = kOEmpty + S;
+  static constexpr int kLEmpty = kLFull + S;
+  static constexpr int kDrain = kLEmpty + S;
+  static constexpr int kNumBars = kDrain + S;
+  static constexpr int kRowStats = (kBars + kNumBars * 8 + 15) / 16 * 16;  // float l[S][128], m[S][128]
+  static constexpr int kMisc = kRowStats + 2 * S * kBlockM * 4;            // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16;
-  static constexpr int kDynamicBytes = kBytes + 1024;  // slack for 1 KB alignment
+  static constexpr int kMaxDynamic = 232448;  // 227 KB per CTA on sm_100
+  // Request 1 KB of alignment slack when it fits; otherwise the kernel relies on the
+  // dynamic shared memory base being 1 KB aligned and checks it.
+  static constexpr int kDynamicBytes = kBytes + 1024 <= kMaxDynamic ? kBytes + 1024 : kBytes;
+  static_assert(kBytes <= kMaxDynamic, "shared-memory plan exceeds 227 KB");
 };
 
 struct WorkItem {
   int b, h, m0;
-  int nb0, nb1;  // K/V tiles needed by query sub-tile 0 / 1 (0 = sub-tile past the end)
+  int nb[2];  // K/V tiles needed by query sub-tile 0 / 1 (0 = sub-tile past the end)
   int nbmax;
-  __device__ __forceinline__ int nb(int i) const { return i == 0 ? nb0 : nb1; }
+  // Runtime-indexed access without a local-memory copy of the array.
+  __device__ __forceinline__ int nbi(int i) const { return i == 0 ? nb[0] : nb[1]; }
 };
 
+template <int SUB>
 __device__ __forceinline__ WorkItem decode_item(int t, const AttnParams& p) {
   const int BH = p.B * p.H;
   const int MB = p.num_mblocks;
@@ -168,15 +202,41 @@ __device__ __forceinline__ WorkItem decode_item(int t, const AttnParams& p) {
   WorkItem it;
   it.b = bh / p.H;
   it.h = bh - it.b * p.H;
-  it.m0 = mb * kItemRows;
+  it.m0 = mb * SUB * kBlockM;
   auto tiles = [&](int r0) {
     if (r0 >= p.N) return 0;
     return p.causal ? min(p.num_kblocks, r0 / kBlockN + 1) : p.num_kblocks;
   };
-  it.nb0 = tiles(it.m0);
-  it.nb1 = tiles(it.m0 + kBlockM);
-  it.nbmax = max(it.nb0, it.nb1);
+  it.nb[0] = tiles(it.m0);
+  it.nb[1] = SUB == 2 ? tiles(it.m0 + kBlockM) : 0;
+  it.nbmax = max(it.nb[0], it.nb[1]);
   return it;
+}
+
+// exp2 on the FMA pipe for a pair of exponents x <= ~9 (-inf never reaches it).
+// Cody-Waite style split x = j + f with j = rint(x) (1.5*2^23 rounding constant) and
+// f = x - j in [-1/2, 1/2] (both exact); 2^f from a degree-3 polynomial with c0 = 1 whose
+// coefficients minimise the maximum relative error on [-1/2, 1/2] (fitted for this
+// kernel by linear programming: 1.0e-4, far below the bf16/fp16 rounding of P; x = 0
+// gives exactly 1); 2^j is added into the exponent bits. x is clamped at -125 so the
+// result stays a normal float.
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr float kExp2C1 = 0.69328290224f;
+constexpr float kExp2C2 = 0.24221095443f;
+constexpr float kExp2C3 = 0.05500892922f;
+
+__device__ __forceinline__ float2 exp2_poly_pair(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = __fadd2_rn(x, make_float2(kRoundMagic, kRoundMagic));    // MAGIC + j
+  const float2 jf = __fadd2_rn(t, make_float2(-kRoundMagic, -kRoundMagic));  // j, exact
+  const float2 f = __fadd2_rn(x, make_float2(-jf.x, -jf.y));                 // x - j, exact
+  float2 pl = __ffma2_rn(make_float2(kExp2C3, kExp2C3), f, make_float2(kExp2C2, kExp2C2));
+  pl = __ffma2_rn(pl, f, make_float2(kExp2C1, kExp2C1));
+  pl = __ffma2_rn(pl, f, make_float2(1.f, 1.f));
+  const int ex = __float_as_int(t.x) << 23;  // j << 23 (the 1.5*2^23 offset shifts out)
+  const int ey = __float_as_int(t.y) << 23;
+  return make_float2(__int_as_float(__float_as_int(pl.x) + ex), __int_as_float(__float_as_int(pl.y) + ey));
 }
 
 // Bounded mbarrier wait. Returns false when the CTA is aborting: either another role
@@ -207,6 +267,11 @@ struct Waiter {
       }
     }
   }
+
+  // Whole-warp form: every lane waits, the result is warp-uniform.
+  __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity) const {
+    return __all_sync(0xffffffffu, wait(bar, parity));
+  }
 };
 
 // Wait used only while tearing down: ignores the abort flag, still bounded; a miss is
@@ -223,51 +288,83 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, unsign
   }
 }
 
-template <int D, typename T, int NS>
-__global__ void __launch_bounds__(kThreads, 1)
+// Position in the K/V ring, as every consumer and the producer walk it. Per item the
+// fills are K(0); then for j = 0 .. nbmax-1: K(j+1) (if j+1 < nbmax), V(j); each K or V
+// tile takes kParts consecutive stages. K runs one tile ahead of V because S(j+1) is
+// issued at the start of softmax(j) while P(j) V(j) waits for its end.
+template <int NS>
+struct Ring {
+  int stage = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++stage == NS) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+};
+
+// EMU8: of every 8 column pairs of an unmasked S tile, how many take exp2 from the
+// FMA-pipe polynomial instead of MUFU (0 = all MUFU).
+template <int D, typename T, int EMU8>
+__global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  static_assert(D == 64 || D == 128, "this kernel covers head dims 64 and 128");
-  using Plan = SmemPlan<D, NS>;
+  using C = Cfg<D>;
+  using Plan = SmemPlan<D>;
+  constexpr int SUB = C::kSub;
+  constexpr int NS = C::kNS;
+  constexpr int KP = C::kParts;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
-  const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
-  uint8_t* smem = smem_raw + (sbase - raw_addr);
+  if (Plan::kDynamicBytes == Plan::kBytes && (raw_addr & 1023u) != 0) {
+    // The plan needs the whole 227 KB and the base is not 1 KB aligned: report, do nothing.
+    if (threadIdx.x == 0) atomicOr(p.status, kStatusSmemAlign);
+    return;
+  }
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  const uint32_t sbase = raw_addr + pad;
+  uint8_t* smem = smem_raw + pad;
 
   const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0);
   const int lane = (int)(threadIdx.x & 31);
+  constexpr int kWarpEpi = 4 * SUB;       // first epilogue warp
+  constexpr int kWarpMma = kWarpEpi + 4;  // first MMA warp
+  constexpr int kWarpProd = kWarpMma + SUB;
 
   auto bar = [&](int slot) -> uint32_t { return sbase + Plan::kBars + slot * 8; };
-  float* row_l = reinterpret_cast<float*>(smem + Plan::kRowStats);          // [2][128]
-  float* row_m = row_l + 2 * kBlockM;                                        // [2][128]
+  float* row_l = reinterpret_cast<float*>(smem + Plan::kRowStats);   // [SUB][128]
+  float* row_m = row_l + SUB * kBlockM;                               // [SUB][128]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Plan::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Plan::kMisc + 4);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       ptx::mbar_init(bar(Plan::kKvFull + s), 1);
-      ptx::mbar_init(bar(Plan::kKvEmpty + s), 1);
+      ptx::mbar_init(bar(Plan::kKvEmpty + s), SUB);  // one release per MMA warp
     }
-    ptx::mbar_init(bar(Plan::kQFull), 1);
-    ptx::mbar_init(bar(Plan::kQEmpty), 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < SUB; ++i) {
+      ptx::mbar_init(bar(Plan::kQFull + i), 1);
+      ptx::mbar_init(bar(Plan::kQEmpty + i), 1);
       ptx::mbar_init(bar(Plan::kSFull + i), 1);
+      ptx::mbar_init(bar(Plan::kSFree + i), kBlockM);
       ptx::mbar_init(bar(Plan::kPFull + i), kBlockM);
+      ptx::mbar_init(bar(Plan::kPFree + i), 1);
       ptx::mbar_init(bar(Plan::kOFull + i), 1);
       ptx::mbar_init(bar(Plan::kOEmpty + i), kBlockM);
       ptx::mbar_init(bar(Plan::kLFull + i), kBlockM);
       ptx::mbar_init(bar(Plan::kLEmpty + i), kBlockM);
+      ptx::mbar_init(bar(Plan::kDrain + i), 1);
     }
-    ptx::mbar_init(bar(Plan::kDrain), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 12) {
+  if (warp == kWarpMma) {
     ptx::tmem_alloc(ptx::smem_u32(tmem_holder), 512);
     ptx::tmem_relinquish();
   }
-  if (warp == 13 && lane == 0) {
+  if (warp == kWarpProd && lane == 0) {
     ptx::prefetch_tmap(&tmQ);
     ptx::prefetch_tmap(&tmK);
     ptx::prefetch_tmap(&tmV);
@@ -278,59 +375,71 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_holder;
   const Waiter W{abort_flag, p.status, p.timeout_ns};
 
-  if (warp < 8) {
+  if (warp < kWarpEpi) {
     // =========================================================== softmax ===
-    ptx::setmaxnreg_inc<kRegsSoftmax>();
-    const int i = warp >> 2;          // sub-tile
-    const int quarter = warp & 3;     // TMEM lane quarter
+    ptx::setmaxnreg_inc<C::kRegsSoftmax>();
+    const int i = warp >> 2;            // sub-tile
+    const int quarter = warp & 3;       // TMEM lane quarter
     const int r = quarter * 32 + lane;  // row within the sub-tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128);
-    const uint32_t tO = tmem + lane_off + (uint32_t)(256 + i * D);
+    const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
+    const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64);
+    // Row r of P in shared memory: two 16 KB chunks (keys 0-63, 64-127) of the SW128
+    // K-major layout; 16-byte unit u of the row sits at unit position u ^ (r & 7).
+    const uint32_t sP = sbase + Plan::kP + i * Plan::kPTileBytes + r * 128;
     const float c = p.scale_log2;
+    const float2 c2 = make_float2(c, c);
     const int kv_last_valid = p.N - (p.num_kblocks - 1) * kBlockN;  // keys in last K tile
-    uint32_t s_par = 0, le_par = 1;
+    uint32_t s_par = 0, le_par = 1, pf_par = 0;
+    int p_written = 0;  // P tiles handed over so far (the buffer is reused every tile)
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
-      const WorkItem it = decode_item(t, p);
-      const int nb = it.nb(i);
+      const WorkItem it = decode_item<SUB>(t, p);
+      const int nb = it.nbi(i);
       if (nb == 0) continue;
       const int diag = (it.m0 + i * kBlockM) / kBlockN;
       float m = 0.f, l = 0.f;
       for (int j = 0; j < nb; ++j) {
-        ok = __all_sync(0xffffffffu, W.wait(bar(Plan::kSFull + i), s_par));
-        if (!ok) break;
+        if (!(ok = W.wait_warp(bar(Plan::kSFull + i), s_par))) break;
         s_par ^= 1;
         ptx::tc_fence_after();
         float s[kBlockN];
+        {
+          uint32_t v[kBlockN / 32][32];
 #pragma unroll
-        for (int ch = 0; ch < kBlockN / 32; ++ch) {
-          uint32_t v[32];
-          ptx::tmem_ld32(tS + ch * 32, v);
+          for (int ch = 0; ch < kBlockN / 32; ++ch) ptx::tmem_ld32(tS + ch * 32, v[ch]);
+          ptx::tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) s[ch * 32 + e] = __uint_as_float(v[e]);
-        }
-        ptx::tmem_wait_ld();
-        if (p.causal) {
-          if (j == diag) {
+          for (int ch = 0; ch < kBlockN / 32; ++ch) {
+            ptx::reg_fence32(v[ch]);  // no use of the loaded values above the wait
 #pragma unroll
-            for (int e = 0; e < kBlockN; ++e)
-              if (e > r) s[e] = -INFINITY;
+            for (int e = 0; e < 32; ++e) s[ch * 32 + e] = __uint_as_float(v[ch][e]);
           }
-        } else if (j == p.num_kblocks - 1 && kv_last_valid < kBlockN) {
+        }
+        // S is in registers: the MMA warp may overwrite it with the next tile's scores.
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(Plan::kSFree + i));
+        const bool diag_tile = p.causal && j == diag;
+        const bool tail_tile = !p.causal && j == p.num_kblocks - 1 && kv_last_valid < kBlockN;
+        const bool masked = diag_tile || tail_tile;  // warp-uniform
+        if (masked) {
+          const int kv_limit = diag_tile ? r + 1 : kv_last_valid;  // keys >= kv_limit masked
 #pragma unroll
           for (int e = 0; e < kBlockN; ++e)
-            if (e >= kv_last_valid) s[e] = -INFINITY;
+            if (e >= kv_limit) s[e] = -INFINITY;
         }
-        float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+        float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+        float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
+        static_assert(kBlockN % 8 == 0, "row max consumes 8 scores per step");
 #pragma unroll
-        for (int e = 4; e < kBlockN; e += 4) {
-          mx0 = fmaxf(mx0, s[e]);
-          mx1 = fmaxf(mx1, s[e + 1]);
-          mx2 = fmaxf(mx2, s[e + 2]);
-          mx3 = fmaxf(mx3, s[e + 3]);
+        for (int e = 8; e < kBlockN; e += 8) {
+          mx0 = ptx::fmax3(mx0, s[e], s[e + 1]);
+          mx1 = ptx::fmax3(mx1, s[e + 2], s[e + 3]);
+          mx2 = ptx::fmax3(mx2, s[e + 4], s[e + 5]);
+          mx3 = ptx::fmax3(mx3, s[e + 6], s[e + 7]);
         }
-        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;  // log2 domain
         float alpha = 1.f;
         bool resc = false;
         if (j == 0) {
@@ -341,62 +450,90 @@ __global__ void __launch_bounds__(kThreads, 1)
           resc = true;
         }
         l *= alpha;
-        const float nm = -m;
-        float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
+        // p = exp2(s*c - m), packed to 16-bit pairs: pk[key half][32]
+        const float2 nm2 = make_float2(-m, -m);
+        float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
+        uint32_t pk[2][32];
+        auto exp_half = [&](const int half, auto poly) {
+          constexpr bool kPoly = decltype(poly)::value;
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float p0 = ptx::ex2(fmaf(s[half * 64 + 2 * e], c, nm));
-            const float p1 = ptx::ex2(fmaf(s[half * 64 + 2 * e + 1], c, nm));
-            sum0 += p0;
-            sum1 += p1;
-            pk[e] = DType<T>::pack(p0, p1);
+            const float2 x = __ffma2_rn(make_float2(s[half * 64 + 2 * e], s[half * 64 + 2 * e + 1]), c2, nm2);
+            float2 pr;
+            if (kPoly && (e & 7) < EMU8) pr = exp2_poly_pair(x);
+            else pr = make_float2(ptx::ex2(x.x), ptx::ex2(x.y));
+            if (e & 1) sb = __fadd2_rn(sb, pr);
+            else sa = __fadd2_rn(sa, pr);
+            pk[half][e] = DType<T>::pack(pr.x, pr.y);
           }
-          ptx::tmem_st32(tS + half * 32, pk);
+        };
+        if (masked) {  // masked keys hold -inf: MUFU gives exactly 0 for them
+          exp_half(0, std::false_type{});
+          exp_half(1, std::false_type{});
+        } else {
+          exp_half(0, std::integral_constant<bool, (EMU8 > 0)>{});
+          exp_half(1, std::integral_constant<bool, (EMU8 > 0)>{});
         }
-        l += sum0 + sum1;
+        const float2 sum = __fadd2_rn(sa, sb);
+        l += sum.x + sum.y;
+        // The P buffer and O are free once the previous P.V of this sub-tile completed.
+        if (p_written > 0) {
+          if (!(ok = W.wait_warp(bar(Plan::kPFree + i), pf_par))) break;
+          pf_par ^= 1;
+        }
+        ++p_written;
+        ptx::tc_fence_after();
         if (__any_sync(0xffffffffu, resc)) {
-          // Done after S is dead to keep register pressure low. O is quiescent here:
-          // the previous P.V of this sub-tile completed before this S tile was
-          // signalled, and the next one waits for our P.
-#pragma unroll
+          // O is quiescent: the previous P.V completed (above) and the next waits for P.
+#pragma unroll 1
           for (int ch = 0; ch < D / 32; ++ch) {
             uint32_t v[32];
             ptx::tmem_ld32(tO + ch * 32, v);
             ptx::tmem_wait_ld();
+            ptx::reg_fence32(v);
 #pragma unroll
             for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
             ptx::tmem_st32(tO + ch * 32, v);
           }
         }
-        ptx::tmem_wait_st();
+        if (C::kPInTmem) {
+          ptx::tmem_st32(tP, pk[0]);
+          ptx::tmem_st32(tP + 32, pk[1]);
+          ptx::tmem_wait_st();
+        } else {
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              ptx::st_shared_v4(sP + h * Plan::kChunkBytes + ((u ^ (r & 7)) << 4), pk[h][4 * u],
+                                pk[h][4 * u + 1], pk[h][4 * u + 2], pk[h][4 * u + 3]);
+          ptx::fence_proxy_async_smem();
+          ptx::tmem_wait_st();  // the O rescale stores, if any
+        }
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(Plan::kPFull + i));
       }
       if (!ok) break;
-      ok = __all_sync(0xffffffffu, W.wait(bar(Plan::kLEmpty + i), le_par));
-      if (!ok) break;
+      if (!(ok = W.wait_warp(bar(Plan::kLEmpty + i), le_par))) break;
       le_par ^= 1;
       row_l[i * kBlockM + r] = l;
       row_m[i * kBlockM + r] = m;
       ptx::mbar_arrive(bar(Plan::kLFull + i));
     }
-  } else if (warp < 12) {
+  } else if (warp < kWarpMma) {
     // ========================================================== epilogue ===
-    ptx::setmaxnreg_dec<kRegsEpilogue>();
+    ptx::setmaxnreg_dec<C::kRegsEpilogue>();
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint32_t lf_par = 0, of_par = 0;  // bit i: barrier parity for sub-tile i
     auto finish = [&](const WorkItem& it, const int i) -> bool {
-      if (!__all_sync(0xffffffffu, W.wait(bar(Plan::kLFull + i), (lf_par >> i) & 1u))) return false;
+      if (!W.wait_warp(bar(Plan::kLFull + i), (lf_par >> i) & 1u)) return false;
       lf_par ^= 1u << i;
       const float l = row_l[i * kBlockM + r];
       const float m = row_m[i * kBlockM + r];
       ptx::mbar_arrive(bar(Plan::kLEmpty + i));
-      if (!__all_sync(0xffffffffu, W.wait(bar(Plan::kOFull + i), (of_par >> i) & 1u))) return false;
+      if (!W.wait_warp(bar(Plan::kOFull + i), (of_par >> i) & 1u)) return false;
       of_par ^= 1u << i;
       ptx::tc_fence_after();
       const float inv = 1.f / l;
@@ -404,12 +541,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = row < p.N;
       T* orow = reinterpret_cast<T*>(p.o) + (long long)it.b * p.o_sb + (long long)it.h * p.o_sh +
                 (long long)row * p.o_sn;
-      const uint32_t tO = tmem + lane_off + (uint32_t)(256 + i * D);
-#pragma unroll
+      const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
+#pragma unroll 1
       for (int ch = 0; ch < D / 32; ++ch) {
         uint32_t v[32];
         ptx::tmem_ld32(tO + ch * 32, v);
         ptx::tmem_wait_ld();
+        ptx::reg_fence32(v);
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
@@ -429,170 +567,194 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
-      const WorkItem it = decode_item(t, p);
-      if (it.nb0 > 0) ok = finish(it, 0);
-      if (ok && it.nb1 > 0) ok = finish(it, 1);
+      const WorkItem it = decode_item<SUB>(t, p);
+      for (int i = 0; i < SUB && ok; ++i)
+        if (it.nbi(i) > 0) ok = finish(it, i);
     }
   } else {
-    ptx::setmaxnreg_dec<kRegsOther>();
-    if (warp == 12) {
+    ptx::setmaxnreg_dec<C::kRegsOther>();
+    if (warp < kWarpMma + SUB) {
       // =============================================================== MMA ===
+      // Warp i issues every MMA of query sub-tile i: S_i(j) = Q_i K(j)^T once softmax i
+      // has read S_i(j-1), and O_i += P_i(j) V(j) once softmax i has written P_i(j). The
+      // whole warp runs the issue path and elect.sync picks the issuing lane (lane 0), so
+      // MMAs and their commits come from one thread.
+      const int i = warp - kWarpMma;
       constexpr uint32_t idS = make_idesc<T>(kBlockM, kBlockN, false);
-      constexpr uint32_t idPV = make_idesc<T>(kBlockM, D, true);
-      const uint32_t sQ = sbase + Plan::kQ;
+      constexpr uint32_t idPV = make_idesc<T>(kBlockM, C::kStageCols, true);
+      const uint32_t sQ = sbase + Plan::kQ + i * Plan::kQTileBytes;
       const uint32_t sKV = sbase + Plan::kKV;
-      int stage = 0;
-      uint32_t kv_par = 0, q_par = 0;
-      uint32_t p_par = 0, oe_par = 3;  // bit i: barrier parity for sub-tile i
+      const uint32_t sPi = sbase + Plan::kP + i * Plan::kPTileBytes;
+      const uint32_t tSi = tmem + (uint32_t)(i * 128);
+      const uint32_t tOi = tmem + (uint32_t)(C::kTmemO + i * D);
+      const uint32_t tPi = tmem + (uint32_t)(C::kTmemP + i * 64);
+      Ring<NS> ring;
+      uint32_t q_par = 0, sf_par = 0, pf_par = 0, oe_par = 0;  // O-empty is first waited on for item 2
+      int s_issued = 0;    // S tiles issued (the S buffer is reused every tile)
+      bool first_item = true;
       bool ok = true;
-      auto issue_S = [&](int i, int st) {
-        const uint64_t a0 = make_sdesc_sw128(sQ + i * Plan::kTileBytes, 16, 1024);
-        const uint64_t b0 = make_sdesc_sw128(sKV + st * Plan::kTileBytes, 16, 1024);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (uint32_t)((kk >> 2) * Plan::kChunkBytes + (kk & 3) * 32) >> 4;
-          ptx::umma_ss(tmem + (uint32_t)(i * 128), a0 + off, b0 + off, idS, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_PV = [&](int i, int st, bool acc) {
-        const uint64_t b0 = make_sdesc_sw128(sKV + st * Plan::kTileBytes, Plan::kChunkBytes, 1024);
-#pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          const uint32_t off = (uint32_t)(kk * 16 * 128) >> 4;
-          ptx::umma_ts(tmem + (uint32_t)(256 + i * D), tmem + (uint32_t)(i * 128 + kk * 8), b0 + off,
-                       idPV, (acc || kk > 0) ? 1u : 0u);
-        }
-      };
-      auto next_stage = [&]() {
-        if (++stage == NS) {
-          stage = 0;
-          kv_par ^= 1;
-        }
-      };
-      // O_i += P_i V_j once softmax i published P_i (and, on an item's first tile, once
-      // the epilogue released O_i).
-      auto pv_step = [&](const int i, int j, int nbi, int sV) -> bool {
-        if (!__all_sync(0xffffffffu, W.wait(bar(Plan::kPFull + i), (p_par >> i) & 1u))) return false;
-        p_par ^= 1u << i;
-        if (j == 0) {
-          if (!__all_sync(0xffffffffu, W.wait(bar(Plan::kOEmpty + i), (oe_par >> i) & 1u))) return false;
-          oe_par ^= 1u << i;
-        }
+      auto acquire = [&]() -> int {
+        const int st = ring.stage;
+        const uint32_t ph = ring.phase;
+        ring.next();
+        if (!W.wait_warp(bar(Plan::kKvFull + st), ph)) return -1;
         ptx::tc_fence_after();
-        if (lane == 0) {
-          issue_PV(i, sV, j > 0);
-          if (j == nbi - 1) ptx::tc_commit(bar(Plan::kOFull + i));
-        }
+        return st;
+      };
+      auto release_unused = [&](int st) {  // a stage this sub-tile does not read
+        if (lane == 0) ptx::mbar_arrive(bar(Plan::kKvEmpty + st));
         __syncwarp();
+      };
+      // S_i(j): kParts stages of K, each contributing its head-dim slice.
+      auto do_S = [&](bool needed) -> bool {
+        if (needed && s_issued > 0) {
+          if (!W.wait_warp(bar(Plan::kSFree + i), sf_par)) return false;
+          sf_par ^= 1;
+        }
+#pragma unroll
+        for (int h = 0; h < KP; ++h) {
+          const int st = acquire();
+          if (st < 0) return false;
+          if (!needed) {
+            release_unused(st);
+            continue;
+          }
+          const uint64_t a0 = make_sdesc_sw128(sQ + h * (C::kStageCols / 64) * Plan::kChunkBytes, 16, 1024);
+          const uint64_t b0 = make_sdesc_sw128(sKV + st * Plan::kStageBytes, 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < C::kStageCols / 16; ++kk) {
+            const uint32_t off = (uint32_t)((kk >> 2) * Plan::kChunkBytes + (kk & 3) * 32) >> 4;
+            ptx::umma_ss_warp(tSi, a0 + off, b0 + off, idS, (h > 0 || kk > 0) ? 1u : 0u);
+          }
+          ptx::tc_commit_warp(bar(Plan::kKvEmpty + st));
+        }
+        if (needed) {
+          ptx::tc_commit_warp(bar(Plan::kSFull + i));
+          ++s_issued;
+        }
         return true;
       };
-      // S_i = Q_i K_{j+1}^T; the K tile is acquired by the first sub-tile that needs it.
-      auto s_step = [&](const int i, int& sK) -> bool {
-        if (sK < 0) {
-          sK = stage;
-          if (!__all_sync(0xffffffffu, W.wait(bar(Plan::kKvFull + sK), kv_par))) return false;
-          next_stage();
-          ptx::tc_fence_after();
+      // O_i (+)= P_i(j) V(j): kParts stages of V, each producing its head-dim slice of O.
+      auto do_PV = [&](bool needed, int j, bool last) -> bool {
+        if (needed) {
+          if (j == 0 && !first_item) {  // the epilogue must have drained O_i
+            if (!W.wait_warp(bar(Plan::kOEmpty + i), oe_par)) return false;
+            oe_par ^= 1;
+          }
+          if (!W.wait_warp(bar(Plan::kPFull + i), pf_par)) return false;
+          pf_par ^= 1;
         }
-        if (lane == 0) {
-          issue_S(i, sK);
-          ptx::tc_commit(bar(Plan::kSFull + i));
+#pragma unroll
+        for (int h = 0; h < KP; ++h) {
+          const int st = acquire();
+          if (st < 0) return false;
+          if (!needed) {
+            release_unused(st);
+            continue;
+          }
+          const uint64_t b0 = make_sdesc_sw128(sKV + st * Plan::kStageBytes, Plan::kChunkBytes, 1024);
+          const uint32_t dO = tOi + (uint32_t)(h * C::kStageCols);
+#pragma unroll
+          for (int kk = 0; kk < kBlockN / 16; ++kk) {
+            const uint32_t boff = (uint32_t)(kk * 16 * 128) >> 4;
+            const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+            if (C::kPInTmem) {
+              ptx::umma_ts_warp(dO, tPi + (uint32_t)(kk * 8), b0 + boff, idPV, acc);
+            } else {
+              const uint64_t a = make_sdesc_sw128(sPi + (kk >> 2) * Plan::kChunkBytes + (kk & 3) * 32, 16, 1024);
+              ptx::umma_ss_warp(dO, a, b0 + boff, idPV, acc);
+            }
+          }
+          ptx::tc_commit_warp(bar(Plan::kKvEmpty + st));
         }
-        __syncwarp();
+        if (needed) {
+          ptx::tc_commit_warp(bar(Plan::kPFree + i));
+          if (last) ptx::tc_commit_warp(bar(Plan::kOFull + i));
+        }
         return true;
       };
       for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
-        const WorkItem it = decode_item(t, p);
-        ok = __all_sync(0xffffffffu, W.wait(bar(Plan::kQFull), q_par));
-        if (!ok) break;
-        q_par ^= 1;
-        int sK = -1;
-        if (it.nb0 > 0) ok = s_step(0, sK);
-        if (ok && it.nb1 > 0) ok = s_step(1, sK);
-        if (!ok) break;
-        if (lane == 0) {
-          ptx::tc_commit(bar(Plan::kKvEmpty + sK));
-          if (it.nbmax == 1) ptx::tc_commit(bar(Plan::kQEmpty));
+        const WorkItem it = decode_item<SUB>(t, p);
+        const int nb = it.nbi(i);
+        if (nb > 0) {
+          if (!(ok = W.wait_warp(bar(Plan::kQFull + i), q_par))) break;
+          q_par ^= 1;
         }
-        __syncwarp();
+        ok = do_S(nb > 0);  // K(0)
+        if (ok && nb == 1) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last use of Q_i
         for (int j = 0; j < it.nbmax && ok; ++j) {
-          const int sV = stage;
-          ok = __all_sync(0xffffffffu, W.wait(bar(Plan::kKvFull + sV), kv_par));
-          if (!ok) break;
-          next_stage();
-          sK = -1;
-          if (j < it.nb0) ok = pv_step(0, j, it.nb0, sV);
-          if (ok && j + 1 < it.nb0) ok = s_step(0, sK);
-          if (ok && j < it.nb1) ok = pv_step(1, j, it.nb1, sV);
-          if (ok && j + 1 < it.nb1) ok = s_step(1, sK);
-          if (!ok) break;
-          if (lane == 0) {
-            ptx::tc_commit(bar(Plan::kKvEmpty + sV));
-            if (sK >= 0) {
-              ptx::tc_commit(bar(Plan::kKvEmpty + sK));
-              if (j + 2 == it.nbmax) ptx::tc_commit(bar(Plan::kQEmpty));
-            }
+          if (j + 1 < it.nbmax) {
+            ok = do_S(j + 1 < nb);  // K(j+1)
+            if (ok && j + 2 == nb) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last S_i
           }
-          __syncwarp();
+          if (ok) ok = do_PV(j < nb, j, j == nb - 1);  // V(j)
         }
+        if (nb > 0) first_item = false;
       }
-      // All MMAs issued by this thread (and their commit arrivals) must land before the
-      // CTA releases TMEM and shared memory.
-      if (lane == 0) {
-        ptx::tc_commit(bar(Plan::kDrain));
-        drain_wait(bar(Plan::kDrain), 0, p.timeout_ns, p.status);
-      }
+      // Every MMA this warp issued (and their commit arrivals) must land before the CTA
+      // releases TMEM and shared memory.
+      ptx::tc_commit_warp(bar(Plan::kDrain + i));
+      if (lane == 0) drain_wait(bar(Plan::kDrain + i), 0, p.timeout_ns, p.status);
       __syncwarp();
-    } else if (warp == 13) {
-      // ========================================================= producer ===
+    } else if (warp < kWarpProd + SUB) {
+      // ========================================================= producers ===
+      // Producer q loads Q of sub-tile q for every item; producer 0 also fills the K/V
+      // ring. Each Q buffer is refilled as soon as its own MMA warp issued the item's last
+      // S, so a sub-tile starts the next item while the other is still finishing.
       if (lane == 0) {
+        const int qi = warp - kWarpProd;
         const uint64_t pol_q = ptx::policy_evict_first();
         const uint64_t pol_kv = ptx::policy_evict_last();
-        const uint32_t sQ = sbase + Plan::kQ;
+        const uint32_t sQ = sbase + Plan::kQ + qi * Plan::kQTileBytes;
         const uint32_t sKV = sbase + Plan::kKV;
-        int stage = 0;
-        uint32_t kv_par = 0, qe_par = 1;
+        Ring<NS> ring;
+        uint32_t qe_par = 1;
         int fills = 0;  // K/V stage fills issued
         bool q_filled = false;
         bool ok = true;
-        for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
-          const WorkItem it = decode_item(t, p);
-          if (!(ok = W.wait(bar(Plan::kQEmpty), qe_par))) break;
-          qe_par ^= 1;
-          const int nq = (it.nb0 > 0) + (it.nb1 > 0);
-          ptx::mbar_arrive_expect_tx(bar(Plan::kQFull), (uint32_t)(nq * Plan::kTileBytes));
-          q_filled = true;
-          for (int i = 0; i < 2; ++i) {
-            if (it.nb(i) == 0) continue;
-            for (int cc = 0; cc < D / 64; ++cc)
-              ptx::tma_load_4d(sQ + i * Plan::kTileBytes + cc * Plan::kChunkBytes, &tmQ,
-                               bar(Plan::kQFull), cc * 64, it.m0 + i * kBlockM, it.h, it.b, pol_q);
+        auto fill = [&](const CUtensorMap* map, int j, int h_idx, int b_idx) -> bool {
+          for (int h = 0; h < KP; ++h) {
+            const int st = ring.stage;
+            const uint32_t ph = ring.phase;
+            ring.next();
+            if (!W.wait(bar(Plan::kKvEmpty + st), ph ^ 1)) return false;
+            ptx::mbar_arrive_expect_tx(bar(Plan::kKvFull + st), (uint32_t)Plan::kStageBytes);
+#pragma unroll
+            for (int cc = 0; cc < C::kStageCols / 64; ++cc)
+              ptx::tma_load_4d(sKV + st * Plan::kStageBytes + cc * Plan::kChunkBytes, map,
+                               bar(Plan::kKvFull + st), h * C::kStageCols + cc * 64, j * kBlockN,
+                               h_idx, b_idx, pol_kv);
+            ++fills;
           }
+          return true;
+        };
+        for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
+          const WorkItem it = decode_item<SUB>(t, p);
+          if (it.nbi(qi) > 0) {
+            if (!(ok = W.wait(bar(Plan::kQEmpty + qi), qe_par))) break;
+            qe_par ^= 1;
+            ptx::mbar_arrive_expect_tx(bar(Plan::kQFull + qi), (uint32_t)Plan::kQTileBytes);
+            for (int cc = 0; cc < D / 64; ++cc)
+              ptx::tma_load_4d(sQ + cc * Plan::kChunkBytes, &tmQ, bar(Plan::kQFull + qi), cc * 64,
+                               it.m0 + qi * kBlockM, it.h, it.b, pol_q);
+            q_filled = true;
+          }
+          if (qi != 0) continue;
+          ok = fill(&tmK, 0, it.h, it.b);
           for (int j = 0; j < it.nbmax && ok; ++j) {
-            for (int kv = 0; kv < 2; ++kv) {
-              if (!(ok = W.wait(bar(Plan::kKvEmpty + stage), kv_par ^ 1))) break;
-              ptx::mbar_arrive_expect_tx(bar(Plan::kKvFull + stage), (uint32_t)Plan::kTileBytes);
-              for (int cc = 0; cc < D / 64; ++cc)
-                ptx::tma_load_4d(sKV + stage * Plan::kTileBytes + cc * Plan::kChunkBytes,
-                                 kv ? (const void*)&tmV : (const void*)&tmK, bar(Plan::kKvFull + stage),
-                                 cc * 64, j * kBlockN, it.h, it.b, pol_kv);
-              ++fills;
-              if (++stage == NS) {
-                stage = 0;
-                kv_par ^= 1;
-              }
-            }
+            if (j + 1 < it.nbmax) ok = fill(&tmK, j + 1, it.h, it.b);
+            if (ok) ok = fill(&tmV, j, it.h, it.b);
           }
         }
-        // Let every load this thread issued land before the CTA exits (normally they
-        // were all consumed already and these waits return at once).
+        // Let every load this thread issued land before the CTA exits (normally they were
+        // all consumed already and these waits return at once).
         const int last = fills < NS ? fills : NS;
         for (int k = 0; k < last; ++k) {
           const int f = fills - 1 - k;  // fill index
           drain_wait(bar(Plan::kKvFull + (f % NS)), (uint32_t)((f / NS) & 1), p.timeout_ns, p.status);
         }
         // qe_par equals the parity of the last Q fill's phase (it flips once per fill).
-        if (q_filled) drain_wait(bar(Plan::kQFull), qe_par, p.timeout_ns, p.status);
+        if (q_filled) drain_wait(bar(Plan::kQFull + qi), qe_par, p.timeout_ns, p.status);
       }
       __syncwarp();
     }
@@ -600,7 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 12) {
+  if (warp == kWarpMma) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, 512);
   }

@@ -235,6 +235,19 @@ __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
                  "+r"(r[31]));
 }
 
+// ----------------------------------------------------------- shared memory --
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the async proxy
+// (tensor-core operand reads) ordered after a subsequent barrier arrive.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ------------------------------------------------------------ misc math -----
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;

@@ -66,25 +66,25 @@ SMALL = [(1, 1, 1), (1, 1, 17), (1, 2, 128), (2, 1, 200), (1, 1, 256), (1, 3, 25
          (1, 2, 1024), (1, 1, 1500)]
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [64, 128, 256])
 @pytest.mark.parametrize("B,H,N", SMALL)
 def test_causal_bf16_small(B, H, N, D):
     check_vs_oracle(B, H, N, D, causal=True, seed=N + D)
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [64, 128, 256])
 @pytest.mark.parametrize("B,H,N", [(1, 1, 1), (1, 2, 100), (2, 1, 256), (1, 1, 700)])
 def test_noncausal_bf16_small(B, H, N, D):
     check_vs_oracle(B, H, N, D, causal=False, seed=7 * N + D)
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [64, 128, 256])
 @pytest.mark.parametrize("causal", [True, False])
 def test_fp16(D, causal):
     check_vs_oracle(2, 2, 333, D, causal=causal, dtype="float16", seed=11)
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [64, 128, 256])
 def test_large_logits_stay_finite(D):
     # q scaled x8: logits far beyond where the reference's rescale-free exp2 overflows
     # in fp16 (fused_attention.py:66,78); the rescaling softmax must stay exact.
@@ -140,6 +140,16 @@ def test_full_size_configs(name, B, H, N, D):
     assert lerr <= LSE_TOL
 
 
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_causal_first_row_is_exactly_v0(D):
+    """Row 0 of causal attention sees only key 0: its softmax weight is exactly 1, so the
+    output must equal v[..., 0, :] bit for bit, in every head (a size-independent property
+    that also catches a wrong row max)."""
+    q, k, v = (t.cuda() for t in make_inputs(4, 8, 1024, D, seed=6))
+    o, _ = run(q, k, v)
+    assert torch.equal(o[:, :, 0], v[:, :, 0])
+
+
 def test_deterministic_bitwise():
     q, k, v = (t.cuda() for t in make_inputs(2, 4, 2048, 128, seed=1))
     o1, l1 = run(q, k, v)
@@ -147,7 +157,7 @@ def test_deterministic_bitwise():
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [64, 128, 256])
 def test_strided_bshd_view_matches_contiguous(D):
     # [B, N, H, D] storage viewed as [B, H, N, D]: served by the tensor maps without a copy.
     B, H, N = 2, 3, 333

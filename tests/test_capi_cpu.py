@@ -52,7 +52,7 @@ def test_strerror_covers_every_code(lib):
 
 def test_version_and_head_dims(lib):
     assert lib.apex_attn_version() >= 100
-    for d in (64, 128):
+    for d in (64, 128, 256):
         assert lib.apex_attn_supports_head_dim(d) == 1
     for d in (0, 32, 96, 512):
         assert lib.apex_attn_supports_head_dim(d) == 0
