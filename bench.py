@@ -8,9 +8,10 @@ A "step" is one forward over the whole batch. value = causal FLOP (2*B*H*N^2*d,
 submission.py:235-240) per second over the K timed steps, device-timed with CUDA events,
 inputs resident in HBM (q/k/v = 805 MB, larger than the 126 MB L2, so no flush).
 
-N > 1 (torchrun, one rank per GPU): C5 (B=8, H=64, N=16384, d=128) with batch x heads
-sharded over the ranks (strong scaling, no collective in the timed region), the output
-gathered to rank 0 over NCCL afterwards and spot-checked there.
+N > 1 (torchrun, one rank per GPU): C5 (B=8, H=64, N=16384, d=128), weak scaling over
+batch x heads: each rank owns 64 of its 512 heads (8 ranks = all of C5), with no collective
+in the timed region; the outputs are gathered to rank 0 over NCCL afterwards and sampled
+heads are checked there.
 
 --impl reference: the reference's own math path on the host CPU (torch SDPA in fp32,
 submission.py:223-232, restated in oracle/attention_oracle.py) over a bounded sample of
@@ -42,6 +43,11 @@ CONFIGS = {
     "C5": dict(B=8, H=64, N=16384, D=128),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM traffic of one C3 launch (dram__bytes_read.sum + dram__bytes_write.sum) from an ncu
+# capture of this kernel: 1.677 GB read + 0.260 GB write. Algorithmic bytes of C3: q, k, v
+# read (3 x 268 MB) + o written (268 MB) + fp32 lse (4.2 MB).
+TRAFFIC_C3_BYTES = 1.677466e9 + 0.260146e9
+ALGO_BYTES_C3 = 4 * 4 * 32 * 8192 * 128 * 2 + 4 * 32 * 8192 * 4
 
 
 def flops(c) -> float:
@@ -220,22 +226,27 @@ def shard_inputs(c, h0, h1, device, seed=42):
                  for _ in range(3))
 
 
+HEADS_PER_RANK = 64  # C5 heads per GPU in the multi-GPU run (8 GPUs = all of C5)
+
+
 def run_multi(args, c, rank, world, local_rank):
-    """C5 over `world` GPUs: each rank runs the kernel on its b*h shard, timed on the
-    device, max over ranks; the output is gathered to rank 0 (NCCL) after timing and a
-    sample of heads is checked there against the fp32 reference."""
+    """C5 across `world` GPUs, weak scaling: rank r owns flattened heads [64r, 64r + 64) of
+    C5 (B=8, H=64, N=16384, d=128), so 8 ranks cover all of C5 and per-GPU work is fixed.
+    Each rank runs the kernel on its heads with no inter-GPU traffic; time is CUDA-event
+    time on each rank, max over ranks. After timing the outputs are gathered to rank 0
+    (one NCCL gather) and sampled heads are checked there against the fp32 reference."""
     import datetime
 
     import torch.distributed as dist
     from apex_attn import custom_attention_forward, device_status
-    from apex_attn.shard import gather_to_rank0, shard_heads
+    from apex_attn.shard import gather_to_rank0
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
-        total = c["B"] * c["H"]
-        h0, h1 = shard_heads(total, world, rank)
+        total = HEADS_PER_RANK * world
+        h0, h1 = rank * HEADS_PER_RANK, (rank + 1) * HEADS_PER_RANK
         q, k, v = shard_inputs(c, h0, h1, device)
         stream = torch.cuda.current_stream(device)
         fn = lambda: custom_attention_forward(q, k, v, causal=True)
@@ -256,6 +267,32 @@ def run_multi(args, c, rank, world, local_rank):
         ms = torch.tensor([t0.elapsed_time(t1)], device=device)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         tmax = ms.item()
+
+        # End to end through the public operator: each rank copies its q/k/v shard from
+        # pinned host memory, runs the forward and copies o back, every step.
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        ho = torch.empty(hq.shape, dtype=hq.dtype).pin_memory()
+
+        def e2e_step():
+            qd, kd, vd = (t.to(device, non_blocking=True) for t in (hq, hk, hv))
+            ho.copy_(custom_attention_forward(qd, kd, vd, causal=True), non_blocking=True)
+
+        e2e_steps = max(2, min(args.steps, 5))
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = torch.tensor([e0.elapsed_time(e1)], device=device)
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        del hq, hk, hv, ho
+
         o = fn()
         status = device_status(local_rank)
         full = gather_to_rank0(o.reshape(h1 - h0, c["N"], c["D"]), total, world, rank)
@@ -263,24 +300,35 @@ def run_multi(args, c, rank, world, local_rank):
             sys.path.insert(0, os.path.join(ROOT, "tests"))
             import gpu_ref
             err = 0.0
-            for r in (0, world - 1):
-                s0, s1 = shard_heads(total, world, r)
-                rq, rk, rv = shard_inputs(c, s0, s1, device)
+            for r in sorted({0, world - 1}):
+                s0 = r * HEADS_PER_RANK
+                rq, rk, rv = shard_inputs(c, s0, s0 + HEADS_PER_RANK, device)
                 sel = slice(0, 2)
                 ro, _ = gpu_ref.attention_fp32(rq[:, sel], rk[:, sel], rv[:, sel], causal=True, with_lse=False)
                 err = max(err, (full[s0:s0 + 2].float() - ro[0]).abs().max().item())
-            value = flops(c) * args.steps / (tmax * 1e-3) / 1e12
+            flop_per_rank = 2.0 * HEADS_PER_RANK * c["N"] ** 2 * c["D"]
+            value = flop_per_rank * world * args.steps / (tmax * 1e-3) / 1e12
+            e2e_value = flop_per_rank * world * e2e_steps / (ems.item() * 1e-3) / 1e12
             peaks, peak_kind = load_peaks()
+            per_gpu = value / world
+            shard_bytes = 3 * HEADS_PER_RANK * c["N"] * c["D"] * 2
             line = {
                 "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": tmax / args.steps,
-                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded N(0,1), device RNG)",
-                "config": {"workload": "C5: causal attn fwd B=8 H=64 N=16384 d=128 bf16, b*h sharded",
-                           "global_batch": c["B"], "seq_len": c["N"], "heads": c["H"], "head_dim": c["D"],
-                           "parallelism": f"dp{world} over b*h", "heads_per_rank": h1 - h0},
-                "frac_of_peak_per_gpu": value / world / peaks["bf16_tflops"],
-                "gpu_launches": args.steps,
+                "config": {"workload": f"C5 slice: causal attn fwd, heads [0, {total}) of B=8 H=64 "
+                                       "N=16384 d=128 bf16 (8 GPUs = all of C5), 64 heads per GPU",
+                           "seq_len": c["N"], "head_dim": c["D"], "heads_per_rank": HEADS_PER_RANK,
+                           "parallelism": f"dp{world} over b*h (no collective in the timed region)",
+                           "l2": "per-rank inputs 805 MB > 126 MB L2, no flush"},
+                "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peaks["bf16_tflops"],
+                             "unit": "TFLOP/s", "frac": per_gpu / peaks["bf16_tflops"], "traffic": None,
+                             "peak_source": f"{peak_kind} bf16_tflops, per GPU"},
+                "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": shard_bytes * world,
+                        "d2h_bytes_per_step": shard_bytes // 3 * world,
+                        "ms_per_step": ems.item() / e2e_steps},
+                "gpu_launches": args.steps * world,
                 "clocks": clk.summary(),
                 "parity": {"max_abs_err_sampled_heads": err, "tol": 1e-2},
                 "device_status": status,
@@ -312,16 +360,25 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        c = CONFIGS["C3"] if args.gpus == 1 else CONFIGS["C5"]
+        # The same workload as this arm's GPU line: C3 on one GPU; on N GPUs, 64 heads of C5
+        # per GPU (the CPU samples heads of that shape; the metric is per-head work/time).
+        n = max(args.gpus, world)
+        if n == 1:
+            c, workload = CONFIGS["C3"], "C3: causal attn fwd B=4 H=32 N=8192 d=128"
+        else:
+            c = dict(B=1, H=HEADS_PER_RANK * n, N=CONFIGS["C5"]["N"], D=CONFIGS["C5"]["D"])
+            workload = f"C5 slice: heads [0, {HEADS_PER_RANK * n}) of B=8 H=64 N=16384 d=128"
         vals = []
         for _ in range(max(1, min(args.steps, 3))):
             v, cores, sample = cpu_reference(c, budget_s=args.cpu_budget / 2)
             vals.append(v)
         value = statistics.median(vals)
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference",
-                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": ("C3 " if args.gpus == 1 else "C5 ") + json.dumps(c)},
+                "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+                "scaling": "weak",
+                "config": {"workload": workload + " (fp32 torch SDPA on the host cores, the "
+                                                  "reference math path, bounded sample of heads)"},
                 "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                                  "sample": sample},
                 "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -350,13 +407,11 @@ def main():
     extra = {}
     for name in ("C2", "C4"):
         c = CONFIGS[name]
-        if apex_attn.supports_head_dim(c["D"]):
-            r = bench_config(name, c, args.steps, args.warmup, device)
-            extra[name] = {"tflops": round(r["tflops"], 1), "ms_per_step": round(r["ms_per_step"], 4),
-                           "frac_of_peak": round(r["tflops"] / peaks["bf16_tflops"], 4),
-                           "config": c}
-        else:
-            extra[name] = {"tflops": None, "note": f"head dim {c['D']} not built"}
+        r = bench_config(name, c, args.steps, args.warmup, device)
+        ach = r["flop_per_step"] / (r["kernel_ms_mean"] * 1e-3) / 1e12
+        extra[name] = {"tflops": round(r["tflops"], 1), "ms_per_step": round(r["ms_per_step"], 4),
+                       "frac_of_peak": round(r["tflops"] / peaks["bf16_tflops"], 4),
+                       "kernel_tflops": round(ach, 1), "config": c}
     e2e = bench_e2e(c3, max(3, min(args.steps, 10)), 3, device)
     status = apex_attn.device_status()
     cpu_v, cores, sample = cpu_reference(c3, budget_s=args.cpu_budget)
@@ -372,8 +427,10 @@ def main():
                    "parallelism": "single GPU", "l2": "inputs 805 MB > 126 MB L2, no flush"},
         "frac_of_peak": res["tflops"] / peak,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None,
-                     "peak_source": f"{peak_kind} bf16_tflops (MEASURED_PEAKS.json)"},
+                     "frac": achieved / peak, "traffic": TRAFFIC_C3_BYTES,
+                     "traffic_unit": "bytes per launch (DRAM read + write, ncu)",
+                     "algorithmic_bytes": ALGO_BYTES_C3,
+                     "peak_source": f"{peak_kind} bf16_tflops (MEASURED_PEAKS.json), kernel timed alone"},
         "cpu_baseline": {"value": cpu_v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": e2e,
