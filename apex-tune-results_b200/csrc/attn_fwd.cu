@@ -13,6 +13,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -42,7 +43,15 @@ template <int D>
 constexpr int kEmu = D == 64 ? APEX_EMU64 : (D == 128 ? APEX_EMU128 : APEX_EMU256);
 
 constexpr int kMaxDevices = 64;
+// Per-device scratch of the kernel: int[64]. Word 0 is the status word; words
+// [kCounterBase, kCounterBase + kCounterSlots) are work-item counters. Each call takes the
+// next slot (round robin) and zeroes it on its stream before the launch, so calls that
+// run concurrently on different streams schedule with different counters.
 constexpr int kStatusBytes = 256;
+constexpr int kCounterBase = 32;
+constexpr int kCounterSlots = 32;
+static_assert((kCounterBase + kCounterSlots) * 4 <= kStatusBytes, "scratch layout");
+std::atomic<unsigned> g_counter_seq{0};
 
 struct DeviceState {
   bool ready = false;
@@ -128,9 +137,10 @@ int init_device(int dev, DeviceState** out) {
 // write on a timeout, lives in the fixed array below instead of a cudaMalloc'd buffer.
 //
 // Every device that loads this library holds this array (256 bytes) until the process
-// exits. The forward kernel needs 4 bytes of it (one status word) whatever B, H, N and D
-// are, so no problem size needs more scratch than the array holds; requests outside the
-// kernel's supported range are rejected with APEX_ATTN_ERR_TOO_LARGE, as by apex_attn_fwd.
+// exits. A launch uses 8 bytes of it (the status word and one work-item counter, in the
+// same layout as the cudaMalloc'd scratch of apex_attn_fwd) whatever B, H, N and D are, so
+// no problem size needs more scratch than the array holds; requests outside the kernel's
+// supported range are rejected with APEX_ATTN_ERR_TOO_LARGE, as by apex_attn_fwd.
 //
 // In host code `g_noalloc_scratch` is only a host-side stand-in for the device array,
 // not a device address: a kernel given it would fault or use the wrong memory. The
@@ -139,7 +149,7 @@ int init_device(int dev, DeviceState** out) {
 // ----------------------------------------------------------------------------
 constexpr int kNoAllocScratchBytes = 256;
 constexpr int kNoAllocStatusBytes = (int)sizeof(int);
-static_assert(kNoAllocStatusBytes <= kNoAllocScratchBytes, "status word must fit the static scratch");
+static_assert(kNoAllocScratchBytes == kStatusBytes, "the static scratch mirrors the allocated one");
 
 static __device__ __align__(256) int g_noalloc_scratch[kNoAllocScratchBytes / sizeof(int)];
 
@@ -309,11 +319,15 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   p.num_mblocks = (int)mblocks;
   p.num_kblocks = (seqlen + apex::kBlockN - 1) / apex::kBlockN;
   p.num_items = (int)(BH * mblocks);
-  // Heads per scheduling group: keep the K/V of the heads that concurrently running CTAs
-  // stream within ~48 MB of L2.
+  // L2 scheduling groups: keep the K/V of the heads that concurrently running CTAs stream
+  // within ~48 MB of L2; split the heads into groups whose sizes differ by at most one.
   const double kv_bytes_per_head = 2.0 * seqlen * head_dim * 2.0;
   long long g = (long long)(48.0 * 1024 * 1024 / kv_bytes_per_head);
-  p.group_heads = (int)std::max(1LL, std::min(g, BH));
+  g = std::max(1LL, std::min(g, BH));
+  const long long ngroups = (BH + g - 1) / g;
+  p.group_q = (int)(BH / ngroups);
+  p.group_big = (int)(BH % ngroups);
+  p.work_counter = ds->status + kCounterBase + (int)(g_counter_seq.fetch_add(1) % kCounterSlots);
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
   p.timeout_ns = wait_timeout_ns();
@@ -327,6 +341,11 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
       (void)cudaGetLastError();
       return APEX_ATTN_ERR_CUDA;
     }
+  }
+  // The work counter must start at zero (ordered before the kernel on the same stream).
+  if (cudaMemsetAsync(p.work_counter, 0, sizeof(int), s) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_CUDA;
   }
   const bool bf16 = dtype == APEX_ATTN_BF16;
   switch (head_dim) {

@@ -60,7 +60,9 @@ struct AttnParams {
   int num_mblocks;   // ceil(N / item rows)
   int num_kblocks;   // ceil(N / 128)
   int num_items;     // B * H * num_mblocks
-  int group_heads;   // heads per L2 scheduling group
+  int group_q;       // L2 scheduling groups hold group_q or group_q + 1 heads ...
+  int group_big;     // ... the first group_big groups hold group_q + 1
+  int* work_counter; // zeroed before the launch; CTAs take item indices from it
   float scale_log2;  // sm_scale * log2(e)
   int causal;
   unsigned long long timeout_ns;
@@ -135,6 +137,10 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr, uint32_t lb
 // 128 rows x 128 bytes with the 128-byte swizzle (16 KB per chunk): the layout the TMA
 // writes and tcgen05.mma reads for K-major operands. The 1 KB-aligned tile region comes
 // first; barriers and row statistics follow it.
+// Work items travel from the scheduling producer to every other role through a ring of
+// kItemRing slots in shared memory.
+constexpr int kItemRing = 4;
+
 template <int D>
 struct SmemPlan {
   using C = Cfg<D>;
@@ -161,9 +167,12 @@ struct SmemPlan {
   static constexpr int kLFull = kOEmpty + S;
   static constexpr int kLEmpty = kLFull + S;
   static constexpr int kDrain = kLEmpty + S;
-  static constexpr int kNumBars = kDrain + S;
+  static constexpr int kItemFull = kDrain + S;          // [kItemRing]
+  static constexpr int kItemEmpty = kItemFull + kItemRing;  // [kItemRing]
+  static constexpr int kNumBars = kItemEmpty + kItemRing;
   static constexpr int kRowStats = (kBars + kNumBars * 8 + 15) / 16 * 16;  // float l[S][128], m[S][128]
-  static constexpr int kMisc = kRowStats + 2 * S * kBlockM * 4;            // tmem base, abort flag
+  static constexpr int kItems = kRowStats + 2 * S * kBlockM * 4;           // int item[kItemRing]
+  static constexpr int kMisc = kItems + kItemRing * 4;                      // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kMaxDynamic = 232448;  // 227 KB per CTA on sm_100
   // Request 1 KB of alignment slack when it fits; otherwise the kernel relies on the
@@ -180,25 +189,31 @@ struct WorkItem {
   __device__ __forceinline__ int nbi(int i) const { return i == 0 ? nb[0] : nb[1]; }
 };
 
+// Item t -> (b, h, query block). Heads are split into L2 groups of group_q or group_q + 1
+// heads (sizes differ by at most one, so no small remainder group comes last); within a
+// group items run longest first (query block descending), heads interleaved. CTAs take
+// items in this order from a shared counter, so long items start early and the small
+// ones fill in at the end.
 template <int SUB>
 __device__ __forceinline__ WorkItem decode_item(int t, const AttnParams& p) {
-  const int BH = p.B * p.H;
   const int MB = p.num_mblocks;
-  const int G = p.group_heads;
-  const int full = BH / G;
-  const int per = G * MB;
-  int mb, bh;
-  if (t < full * per) {
-    const int g = t / per;
-    const int r = t - g * per;
-    mb = MB - 1 - r / G;
-    bh = g * G + r % G;
+  const int q = p.group_q;
+  const int big_items = p.group_big * (q + 1) * MB;
+  int size, base, r;
+  if (t < big_items) {
+    size = q + 1;
+    const int g = t / (size * MB);
+    r = t - g * size * MB;
+    base = g * size;
   } else {
-    const int rem = BH - full * G;
-    const int r = t - full * per;
-    mb = MB - 1 - r / rem;
-    bh = full * G + r % rem;
+    size = q;
+    const int t2 = t - big_items;
+    const int g = t2 / (size * MB);
+    r = t2 - g * size * MB;
+    base = p.group_big * (q + 1) + g * size;
   }
+  const int mb = MB - 1 - r / size;
+  const int bh = base + r % size;
   WorkItem it;
   it.b = bh / p.H;
   it.h = bh - it.b * p.H;
@@ -304,6 +319,30 @@ struct Ring {
   }
 };
 
+// Reader side of the item ring: every role walks the same sequence of item indices that
+// the scheduling producer publishes; index -1 ends the sequence. Each reading warp releases
+// a slot once (lane 0) after reading it.
+struct ItemReader {
+  int k = 0;
+  __device__ __forceinline__ bool next(const Waiter& W, uint32_t full0, uint32_t empty0,
+                                       const int* items, bool whole_warp, int& t) {
+    const int slot = k % kItemRing;
+    const uint32_t parity = (uint32_t)(k / kItemRing) & 1u;
+    ++k;
+    if (whole_warp) {
+      if (!W.wait_warp(full0 + slot * 8, parity)) return false;
+      t = items[slot];
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) ptx::mbar_arrive(empty0 + slot * 8);
+    } else {
+      if (!W.wait(full0 + slot * 8, parity)) return false;
+      t = items[slot];
+      ptx::mbar_arrive(empty0 + slot * 8);
+    }
+    return true;
+  }
+};
+
 // EMU8: of every 8 column pairs of an unmasked S tile, how many take exp2 from the
 // FMA-pipe polynomial instead of MUFU (0 = all MUFU).
 template <int D, typename T, int EMU8>
@@ -336,6 +375,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
   auto bar = [&](int slot) -> uint32_t { return sbase + Plan::kBars + slot * 8; };
   float* row_l = reinterpret_cast<float*>(smem + Plan::kRowStats);   // [SUB][128]
   float* row_m = row_l + SUB * kBlockM;                               // [SUB][128]
+  int* items = reinterpret_cast<int*>(smem + Plan::kItems);           // [kItemRing]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Plan::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Plan::kMisc + 4);
 
@@ -356,6 +396,13 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       ptx::mbar_init(bar(Plan::kLFull + i), kBlockM);
       ptx::mbar_init(bar(Plan::kLEmpty + i), kBlockM);
       ptx::mbar_init(bar(Plan::kDrain + i), 1);
+    }
+    // Readers of the item ring: softmax, epilogue and MMA warps, and the Q producer of
+    // sub-tile 1 (the ring producer writes it).
+    constexpr int kItemReaders = 4 * SUB + 4 + SUB + (SUB - 1);
+    for (int k = 0; k < kItemRing; ++k) {
+      ptx::mbar_init(bar(Plan::kItemFull + k), 1);
+      ptx::mbar_init(bar(Plan::kItemEmpty + k), kItemReaders);
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -394,7 +441,10 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     uint32_t s_par = 0, le_par = 1, pf_par = 0;
     int p_written = 0;  // P tiles handed over so far (the buffer is reused every tile)
     bool ok = true;
-    for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
+    ItemReader reader;
+    while (ok) {
+      int t;
+      if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
       const WorkItem it = decode_item<SUB>(t, p);
       const int nb = it.nbi(i);
       if (nb == 0) continue;
@@ -566,7 +616,10 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       return true;
     };
     bool ok = true;
-    for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
+    ItemReader reader;
+    while (ok) {
+      int t;
+      if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
       const WorkItem it = decode_item<SUB>(t, p);
       for (int i = 0; i < SUB && ok; ++i)
         if (it.nbi(i) > 0) ok = finish(it, i);
@@ -673,7 +726,10 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         }
         return true;
       };
-      for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
+      ItemReader reader;
+      while (ok) {
+        int t;
+        if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
         const WorkItem it = decode_item<SUB>(t, p);
         const int nb = it.nbi(i);
         if (nb > 0) {
@@ -728,7 +784,27 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
           }
           return true;
         };
-        for (int t = blockIdx.x; t < p.num_items && ok; t += gridDim.x) {
+        // Producer 0 schedules: it takes item indices from the shared work counter (one
+        // fetch ahead, so the atomic's latency overlaps the current item) and publishes
+        // them to the item ring; every other role reads the ring.
+        ItemReader reader;
+        int fetched = qi == 0 ? atomicAdd(p.work_counter, 1) : 0;
+        int published = 0;
+        while (ok) {
+          int t;
+          if (qi == 0) {
+            const int slot = published % kItemRing;
+            const uint32_t parity = ((uint32_t)(published / kItemRing) & 1u) ^ 1u;
+            if (!(ok = W.wait(bar(Plan::kItemEmpty + slot), parity))) break;
+            t = fetched < p.num_items ? fetched : -1;
+            if (t >= 0) fetched = atomicAdd(p.work_counter, 1);
+            items[slot] = t;
+            ptx::mbar_arrive(bar(Plan::kItemFull + slot));  // release: publishes the slot
+            ++published;
+          } else if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, false, t))) {
+            break;
+          }
+          if (t < 0) break;
           const WorkItem it = decode_item<SUB>(t, p);
           if (it.nbi(qi) > 0) {
             if (!(ok = W.wait(bar(Plan::kQEmpty + qi), qe_par))) break;

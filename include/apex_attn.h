@@ -11,7 +11,8 @@
  * logical [B, H, N, D] with unit stride along D, strides are given in elements.
  * Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy default
  * stream). No call allocates caller-visible memory; the library keeps one small
- * status word per device for device-side error reporting.
+ * scratch buffer per device (a status word for device-side error reporting and the
+ * work-item counters of its scheduler).
  */
 #ifndef APEX_ATTN_H_
 #define APEX_ATTN_H_
@@ -61,7 +62,8 @@ int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* l
 /*
  * Reads and clears the device status word of `device` after synchronising that
  * device. *flags receives the raw bits (1 = a kernel hit its bounded-wait limit,
- * 2 = a copy or MMA still in flight at kernel teardown did not land within the limit).
+ * 2 = a copy or MMA still in flight at kernel teardown did not land within the limit,
+ * 4 = the dynamic shared-memory base was not 1 KB aligned, so a kernel did nothing).
  * Returns APEX_ATTN_ERR_DEVICE_TIMEOUT when any bit was set.
  * Has no counterpart in the reference (its Triton kernels cannot report device faults).
  */
@@ -82,16 +84,18 @@ int apex_attn_selftest_wait_timeout(int timeout_us, void* stream);
  * host that forbids allocations outside its own allocator, a real-time loop).
  *
  * The caller passes the inputs and outputs as for apex_attn_fwd. The kernel's scratch
- * (its 4-byte device status word) lives in a fixed 256-byte static device array of the
- * library that every device loading the library holds until process exit; this entry
- * point calls no cudaMalloc, cudaFree or other allocating routine. The scratch need does
- * not grow with B, H, N or D; sizes outside the kernel's supported range are rejected
- * with APEX_ATTN_ERR_TOO_LARGE.
+ * (a 4-byte device status word and a 4-byte work-item counter, one of 32 that rotate
+ * between calls) lives in a fixed 256-byte static device array of the library that every
+ * device loading the library holds until process exit; this entry point calls no
+ * cudaMalloc, cudaFree or other allocating routine. The scratch need does not grow with
+ * B, H, N or D; sizes outside the kernel's supported range are rejected with
+ * APEX_ATTN_ERR_TOO_LARGE.
  *
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress)
  * and sets kernel attributes for that device, so make it before any stream capture.
- * Each call clears the status word on `stream` before its kernel. All calls share the
- * array: calls that overlap on the GPU (other streams, other threads) race on it. A
+ * Each call clears the status word and its counter on `stream` before its kernel. All
+ * calls share the array: calls that overlap on the GPU (other streams, other threads)
+ * race on the status word, and on a counter once more than 32 calls are in flight. A
  * bounded wait that expires still ends the kernel early, but its status bit stays in the
  * shared scratch, which apex_attn_device_status does not read; callers that need
  * device-fault reports use apex_attn_fwd.
