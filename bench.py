@@ -43,6 +43,13 @@ CONFIGS = {
     "C5": dict(B=8, H=64, N=16384, D=128),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# The MLS-Bench shapes the reference publishes numbers for (fp16, causal;
+# mls-bench_fused_attention/bench.py:23-27) and its published H100 TFLOP/s for them
+# (results/benchmark_results.json:16,28,40; README.md:13-15).
+MLS_SHAPES = {64: dict(B=4, H=32, N=4096, D=64), 128: dict(B=2, H=16, N=8192, D=128),
+              256: dict(B=1, H=8, N=16384, D=256)}
+PUBLISHED_H100_TFLOPS = {64: 430.7, 128: 468.4, 256: 451.7}
+
 # DRAM traffic of one C3 launch (dram__bytes_read.sum + dram__bytes_write.sum) from an ncu
 # capture of this kernel: 1.677 GB read + 0.260 GB write. Algorithmic bytes of C3: q, k, v
 # read (3 x 268 MB) + o written (268 MB) + fp32 lse (4.2 MB).
@@ -164,6 +171,31 @@ def bench_config(name, c, steps, warmup, device):
     return {"tflops": f * steps / (total_ms * 1e-3) / 1e12, "ms_per_step": total_ms / steps,
             "kernel_ms_median": statistics.median(per), "kernel_ms_mean": sum(per) / len(per),
             "flop_per_step": f}
+
+
+def bench_mls_shapes(steps, warmup, device):
+    """fp16 causal forward at the MLS-Bench shapes: this kernel and torch SDPA on the same
+    GPU (the harness's speedup_vs_sdpa, submission.py:320-333), next to the reference's
+    published H100 numbers."""
+    import torch.nn.functional as F
+    from apex_attn import custom_attention_forward
+    stream = torch.cuda.current_stream(device)
+    out = {}
+    for d, c in MLS_SHAPES.items():
+        g = torch.Generator(device=device).manual_seed(42)
+        shape = (c["B"], c["H"], c["N"], c["D"])
+        q, k, v = (torch.randn(shape, generator=g, device=device, dtype=torch.float16) for _ in range(3))
+        ms, _ = time_device(lambda: custom_attention_forward(q, k, v, causal=True), steps, warmup, stream)
+        sdpa_ms, _ = time_device(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), steps, warmup, stream)
+        f = flops(c)
+        t = f * steps / (ms * 1e-3) / 1e12
+        ts = f * steps / (sdpa_ms * 1e-3) / 1e12
+        out[f"d{d}"] = {"shape": c, "tflops": round(t, 1), "sdpa_tflops_same_gpu": round(ts, 1),
+                        "speedup_vs_sdpa": round(ts and t / ts, 3),
+                        "published_h100_tflops": PUBLISHED_H100_TFLOPS[d],
+                        "vs_published_h100": round(t / PUBLISHED_H100_TFLOPS[d], 3)}
+        del q, k, v
+    return out
 
 
 def bench_e2e(c, steps, warmup, device):
@@ -412,6 +444,7 @@ def main():
         extra[name] = {"tflops": round(r["tflops"], 1), "ms_per_step": round(r["ms_per_step"], 4),
                        "frac_of_peak": round(r["tflops"] / peaks["bf16_tflops"], 4),
                        "kernel_tflops": round(ach, 1), "config": c}
+    mls = bench_mls_shapes(max(3, min(args.steps, 10)), 3, device)
     e2e = bench_e2e(c3, max(3, min(args.steps, 10)), 3, device)
     status = apex_attn.device_status()
     cpu_v, cores, sample = cpu_reference(c3, budget_s=args.cpu_budget)
@@ -437,6 +470,7 @@ def main():
         "gpu_launches": args.steps,
         "clocks": clocks,
         "per_config": extra,
+        "mls_bench_fp16": mls,
         "device_status": status,
     }
     print(json.dumps(line))
