@@ -33,6 +33,16 @@ ERR_CUDA = -12
 DTYPE_BF16 = 0
 DTYPE_FP16 = 1
 
+class FwdArgs(ctypes.Structure):
+    """Mirror of apex_attn_fwd_args (include/apex_attn.h)."""
+    _fields_ = [("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+                ("o", ctypes.c_void_p), ("lse", ctypes.c_void_p), ("batch", ctypes.c_int),
+                ("heads_q", ctypes.c_int), ("heads_kv", ctypes.c_int), ("seqlen", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("dtype", ctypes.c_int), ("causal", ctypes.c_int),
+                ("window_left", ctypes.c_int), ("sm_scale", ctypes.c_float),
+                ("strides", ctypes.c_longlong * 12)]
+
+
 # Every symbol the header declares: (name, restype, argtypes).
 _c_ll_p = ctypes.POINTER(ctypes.c_longlong)
 SYMBOLS = {
@@ -42,6 +52,7 @@ SYMBOLS = {
          ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
          ctypes.c_float, _c_ll_p, ctypes.c_void_p],
     ),
+    "apex_attn_fwd_ex": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.c_void_p]),
     "apex_attn_fwd_noalloc": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

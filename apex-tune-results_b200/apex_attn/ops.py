@@ -11,8 +11,11 @@ defaults, output and error behaviour of the reference operator
 * the result is a new contiguous tensor of q's shape and dtype, produced asynchronously
   on the current CUDA stream (fused_attention.py:161).
 
-Extension beyond the reference: ``return_lse=True`` also returns the fp32 natural-log
-logsumexp ``[batch, nheads, seqlen]``. Inputs whose layout the TMA tensor maps accept
+Extensions beyond the reference:
+* ``return_lse=True`` also returns the fp32 natural-log logsumexp ``[batch, nheads, seqlen]``;
+* grouped-query attention: k and v may have fewer heads than q (a divisor of q's);
+* ``window_left=w`` (causal only): row i attends to keys i - w .. i (a sliding window, as in
+  flash_attn_func(window_size=(w, 0)) at nanochat_autoresearch/solutions/train.py:719). Inputs whose layout the TMA tensor maps accept
 directly (unit head-dim stride, other strides multiples of 8 elements) are not copied;
 others are made contiguous first, like the reference's ``.contiguous()`` (:157).
 """
@@ -48,18 +51,24 @@ def _strides(t: torch.Tensor) -> list[int]:
     return [s if size > 1 else c for size, s, c in zip((b, h, n), t.stride()[:3], contiguous)]
 
 
-def custom_attention_forward(q, k, v, causal=True, sm_scale=None, return_lse=False):
+def custom_attention_forward(q, k, v, causal=True, sm_scale=None, return_lse=False, window_left=None):
     """Causal (or full) attention forward on B200; see the module docstring."""
-    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
-        raise ValueError(f"q, k, v must share one [B, H, N, D] shape, got {tuple(q.shape)}, "
+    if q.dim() != 4 or k.dim() != 4 or k.shape != v.shape:
+        raise ValueError(f"q, k, v must be [B, H, N, D] with k and v alike, got {tuple(q.shape)}, "
                          f"{tuple(k.shape)}, {tuple(v.shape)}")
     batch, nheads, seqlen, headdim = q.shape
+    kv_heads = k.shape[1]
+    if (k.shape[0], k.shape[2], k.shape[3]) != (batch, seqlen, headdim) or nheads % kv_heads != 0:
+        raise ValueError(f"k and v must be [B, H_kv, N, D] with H_kv dividing q's heads, got q "
+                         f"{tuple(q.shape)}, k {tuple(k.shape)}")
     if not supports_head_dim(headdim):
         raise KeyError(headdim)
     if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError(f"q, k, v must all be float16 or bfloat16, got {q.dtype}, {k.dtype}, {v.dtype}")
     if not (q.is_cuda and k.is_cuda and v.is_cuda) or not (q.device == k.device == v.device):
         raise ValueError("q, k, v must be CUDA tensors on one device")
+    if window_left is not None and (window_left < 0 or not causal):
+        raise ValueError("window_left must be >= 0 and needs causal=True")
     q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(headdim)
@@ -67,13 +76,24 @@ def custom_attention_forward(q, k, v, causal=True, sm_scale=None, return_lse=Fal
     lse = torch.empty((batch, nheads, seqlen), dtype=torch.float32, device=q.device) if return_lse else None
     if q.numel() == 0:
         return (o, lse) if return_lse else o
-    strides = (ctypes.c_longlong * 12)(*(_strides(q) + _strides(k) + _strides(v) + _strides(o)))
+    strides = _strides(q) + _strides(k) + _strides(v) + _strides(o)
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    rc = _lib.load().apex_attn_fwd(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-        lse.data_ptr() if lse is not None else None,
-        batch, nheads, seqlen, headdim, _DTYPES[q.dtype], 1 if causal else 0, float(sm_scale),
-        strides, stream)
+    lib = _lib.load()
+    if kv_heads == nheads and window_left is None:
+        # The reference-shaped entry point (fused_attention.py:155-193).
+        rc = lib.apex_attn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+            lse.data_ptr() if lse is not None else None,
+            batch, nheads, seqlen, headdim, _DTYPES[q.dtype], 1 if causal else 0, float(sm_scale),
+            (ctypes.c_longlong * 12)(*strides), stream)
+    else:
+        args = _lib.FwdArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), o=o.data_ptr(),
+                            lse=lse.data_ptr() if lse is not None else None, batch=batch,
+                            heads_q=nheads, heads_kv=kv_heads, seqlen=seqlen, head_dim=headdim,
+                            dtype=_DTYPES[q.dtype], causal=1 if causal else 0,
+                            window_left=-1 if window_left is None else int(window_left),
+                            sm_scale=float(sm_scale), strides=(ctypes.c_longlong * 12)(*strides))
+        rc = lib.apex_attn_fwd_ex(ctypes.byref(args), stream)
     _lib.check(rc, "custom_attention_forward")
     return (o, lse) if return_lse else o
 

@@ -208,10 +208,10 @@ int encode_map(CUtensorMap* m, const void* ptr, int dtype, int B, int H, int N, 
   return r == CUDA_SUCCESS ? APEX_ATTN_OK : APEX_ATTN_ERR_TENSOR_MAP;
 }
 
-template <int D, typename T>
-int launch(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
-           const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
-  auto kern = apex::attn_fwd_sm100_kernel<D, T, kEmu<D>>;
+template <int D, typename T, bool WIN>
+int launch_one(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
+               const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
+  auto kern = apex::attn_fwd_sm100_kernel<D, T, kEmu<D>, WIN>;
   constexpr int smem = apex::SmemPlan<D>::kDynamicBytes;
   if (!(ds.attr_done & attr_bit)) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -224,6 +224,14 @@ int launch(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUte
   kern<<<grid, apex::Cfg<D>::kThreads, smem, stream>>>(mq, mk, mv, p);
   if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
   return APEX_ATTN_OK;
+}
+
+// attr_bit covers the (D, T) pair; the windowed instantiation uses the next bit up.
+template <int D, typename T>
+int launch(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
+           const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
+  if (p.window >= 0) return launch_one<D, T, true>(ds, attr_bit << 8, mq, mk, mv, p, grid, stream);
+  return launch_one<D, T, false>(ds, attr_bit, mq, mk, mv, p, grid, stream);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -272,11 +280,13 @@ bool supported_head_dim(int head_dim) { return head_dim == 64 || head_dim == 128
 // Validation, tensor maps, parameters and dispatch shared by both forward entry points.
 // `noalloc` selects the allocation-free device state and clears its status word first.
 int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, float* lse, int batch,
-            int heads, int seqlen, int head_dim, int dtype, int causal, float sm_scale,
-            const long long* strides, void* stream) {
+            int heads, int heads_kv, int seqlen, int head_dim, int dtype, int causal, int window,
+            float sm_scale, const long long* strides, void* stream) {
   // ---- argument validation (no CUDA calls) ----
   if (!q || !k || !v || !o || !strides) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   if (batch <= 0 || heads <= 0 || seqlen <= 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (heads_kv <= 0 || heads % heads_kv != 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (window < -1 || (window >= 0 && !causal)) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   if (!supported_head_dim(head_dim)) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
   if (dtype != APEX_ATTN_BF16 && dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
   if (!std::isfinite(sm_scale) || !(sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
@@ -302,8 +312,8 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
 
   CUtensorMap mq, mk, mv;
   if ((rc = encode_map(&mq, q, dtype, batch, heads, seqlen, head_dim, strides[0], strides[1], strides[2])) ||
-      (rc = encode_map(&mk, k, dtype, batch, heads, seqlen, head_dim, strides[3], strides[4], strides[5])) ||
-      (rc = encode_map(&mv, v, dtype, batch, heads, seqlen, head_dim, strides[6], strides[7], strides[8])))
+      (rc = encode_map(&mk, k, dtype, batch, heads_kv, seqlen, head_dim, strides[3], strides[4], strides[5])) ||
+      (rc = encode_map(&mv, v, dtype, batch, heads_kv, seqlen, head_dim, strides[6], strides[7], strides[8])))
     return rc;
 
   AttnParams p{};
@@ -320,8 +330,9 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   p.num_kblocks = (seqlen + apex::kBlockN - 1) / apex::kBlockN;
   p.num_items = (int)(BH * mblocks);
   // L2 scheduling groups: keep the K/V of the heads that concurrently running CTAs stream
-  // within ~48 MB of L2; split the heads into groups whose sizes differ by at most one.
-  const double kv_bytes_per_head = 2.0 * seqlen * head_dim * 2.0;
+  // within ~48 MB of L2 (query heads that share a K/V head count once); split the heads
+  // into groups whose sizes differ by at most one.
+  const double kv_bytes_per_head = 2.0 * seqlen * head_dim * 2.0 / (heads / heads_kv);
   long long g = (long long)(48.0 * 1024 * 1024 / kv_bytes_per_head);
   g = std::max(1LL, std::min(g, BH));
   const long long ngroups = (BH + g - 1) / g;
@@ -330,6 +341,8 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   p.work_counter = ds->status + kCounterBase + (int)(g_counter_seq.fetch_add(1) % kCounterSlots);
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
+  p.kv_group = heads / heads_kv;
+  p.window = window;
   p.timeout_ns = wait_timeout_ns();
   const int grid = std::min(p.num_items, ds->num_sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -391,15 +404,21 @@ const char* apex_attn_strerror(int status) {
 int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch,
                   int heads, int seqlen, int head_dim, int dtype, int causal, float sm_scale,
                   const long long* strides, void* stream) {
-  return forward(false, q, k, v, o, lse, batch, heads, seqlen, head_dim, dtype, causal, sm_scale,
-                 strides, stream);
+  return forward(false, q, k, v, o, lse, batch, heads, heads, seqlen, head_dim, dtype, causal, -1,
+                 sm_scale, strides, stream);
+}
+
+int apex_attn_fwd_ex(const apex_attn_fwd_args* a, void* stream) {
+  if (!a) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  return forward(false, a->q, a->k, a->v, a->o, a->lse, a->batch, a->heads_q, a->heads_kv, a->seqlen,
+                 a->head_dim, a->dtype, a->causal, a->window_left, a->sm_scale, a->strides, stream);
 }
 
 int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
                           int batch, int heads, int seqlen, int head_dim, int dtype, int causal,
                           float sm_scale, const long long* strides, void* stream) {
-  return forward(true, q, k, v, o, lse, batch, heads, seqlen, head_dim, dtype, causal, sm_scale,
-                 strides, stream);
+  return forward(true, q, k, v, o, lse, batch, heads, heads, seqlen, head_dim, dtype, causal, -1,
+                 sm_scale, strides, stream);
 }
 
 int apex_attn_device_status(int device, int* flags) {

@@ -65,6 +65,8 @@ struct AttnParams {
   int* work_counter; // zeroed before the launch; CTAs take item indices from it
   float scale_log2;  // sm_scale * log2(e)
   int causal;
+  int kv_group;      // query heads per K/V head (grouped-query attention; 1 = plain)
+  int window;        // causal sliding window: key j visible to row i iff i - window <= j (-1: none)
   unsigned long long timeout_ns;
 };
 
@@ -183,10 +185,12 @@ struct SmemPlan {
 
 struct WorkItem {
   int b, h, m0;
-  int nb[2];  // K/V tiles needed by query sub-tile 0 / 1 (0 = sub-tile past the end)
-  int nbmax;
-  // Runtime-indexed access without a local-memory copy of the array.
+  // Query sub-tile i reads K/V tiles [lo[i], nb[i]); nb[i] = 0: sub-tile past the end.
+  int lo[2], nb[2];
+  int jlo, nbmax;  // K/V tiles of the item: [jlo, nbmax), the union over its sub-tiles
+  // Runtime-indexed access without a local-memory copy of the arrays.
   __device__ __forceinline__ int nbi(int i) const { return i == 0 ? nb[0] : nb[1]; }
+  __device__ __forceinline__ int loi(int i) const { return i == 0 ? lo[0] : lo[1]; }
 };
 
 // Item t -> (b, h, query block). Heads are split into L2 groups of group_q or group_q + 1
@@ -194,7 +198,7 @@ struct WorkItem {
 // group items run longest first (query block descending), heads interleaved. CTAs take
 // items in this order from a shared counter, so long items start early and the small
 // ones fill in at the end.
-template <int SUB>
+template <int SUB, bool WIN>
 __device__ __forceinline__ WorkItem decode_item(int t, const AttnParams& p) {
   const int MB = p.num_mblocks;
   const int q = p.group_q;
@@ -222,9 +226,15 @@ __device__ __forceinline__ WorkItem decode_item(int t, const AttnParams& p) {
     if (r0 >= p.N) return 0;
     return p.causal ? min(p.num_kblocks, r0 / kBlockN + 1) : p.num_kblocks;
   };
+  // First K/V tile a sub-tile starting at row r0 can see: with a sliding window, row r0
+  // sees keys >= r0 - window (later rows see fewer low keys, masked per element).
+  auto first = [&](int r0) { return WIN ? max(0, r0 - p.window) / kBlockN : 0; };
   it.nb[0] = tiles(it.m0);
   it.nb[1] = SUB == 2 ? tiles(it.m0 + kBlockM) : 0;
+  it.lo[0] = first(it.m0);
+  it.lo[1] = SUB == 2 ? first(it.m0 + kBlockM) : 0;
   it.nbmax = max(it.nb[0], it.nb[1]);
+  it.jlo = it.lo[0];  // lo[1] >= lo[0] whenever sub-tile 1 has tiles
   return it;
 }
 
@@ -345,7 +355,9 @@ struct ItemReader {
 
 // EMU8: of every 8 column pairs of an unmasked S tile, how many take exp2 from the
 // FMA-pipe polynomial instead of MUFU (0 = all MUFU).
-template <int D, typename T, int EMU8>
+// WIN: the launch uses a causal sliding window (p.window >= 0); without it the window
+// logic compiles away.
+template <int D, typename T, int EMU8, bool WIN>
 __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
@@ -445,12 +457,14 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     while (ok) {
       int t;
       if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-      const WorkItem it = decode_item<SUB>(t, p);
+      const WorkItem it = decode_item<SUB, WIN>(t, p);
       const int nb = it.nbi(i);
+      const int lo = it.loi(i);
       if (nb == 0) continue;
-      const int diag = (it.m0 + i * kBlockM) / kBlockN;
+      const int r0 = it.m0 + i * kBlockM;  // first row of the sub-tile
+      const int diag = r0 / kBlockN;
       float m = 0.f, l = 0.f;
-      for (int j = 0; j < nb; ++j) {
+      for (int j = lo; j < nb; ++j) {
         if (!(ok = W.wait_warp(bar(Plan::kSFull + i), s_par))) break;
         s_par ^= 1;
         ptx::tc_fence_after();
@@ -472,12 +486,16 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         ptx::mbar_arrive(bar(Plan::kSFree + i));
         const bool diag_tile = p.causal && j == diag;
         const bool tail_tile = !p.causal && j == p.num_kblocks - 1 && kv_last_valid < kBlockN;
-        const bool masked = diag_tile || tail_tile;  // warp-uniform
+        // Sliding window: the tile holds keys below some row's window start iff its first
+        // key is below the sub-tile's last row minus the window.
+        const bool win_tile = WIN && j * kBlockN < r0 + kBlockM - 1 - p.window;
+        const bool masked = diag_tile || tail_tile || win_tile;  // warp-uniform
         if (masked) {
-          const int kv_limit = diag_tile ? r + 1 : kv_last_valid;  // keys >= kv_limit masked
+          const int kv_limit = diag_tile ? r + 1 : (tail_tile ? kv_last_valid : kBlockN);  // keys >= limit masked
+          const int kv_first = win_tile ? r0 + r - p.window - j * kBlockN : 0;            // keys < first masked
 #pragma unroll
           for (int e = 0; e < kBlockN; ++e)
-            if (e >= kv_limit) s[e] = -INFINITY;
+            if (e >= kv_limit || e < kv_first) s[e] = -INFINITY;
         }
         float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
         float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
@@ -492,16 +510,17 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;  // log2 domain
         float alpha = 1.f;
         bool resc = false;
-        if (j == 0) {
-          m = mx;
-        } else if (mx > m + kRescaleLog2) {
+        if (j == lo) {
+          m = mx;  // -inf when the window hides this whole tile from the row
+        } else if (mx > m + kRescaleLog2) {  // from m = -inf: alpha = 0, as it must be
           alpha = ptx::ex2(m - mx);
           m = mx;
           resc = true;
         }
         l *= alpha;
         // p = exp2(s*c - m), packed to 16-bit pairs: pk[key half][32]
-        const float2 nm2 = make_float2(-m, -m);
+        const float m_use = (WIN && m == -INFINITY) ? 0.f : m;  // all keys masked: p = 0, not NaN
+        const float2 nm2 = make_float2(-m_use, -m_use);
         float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
         uint32_t pk[2][32];
         auto exp_half = [&](const int half, auto poly) {
@@ -620,7 +639,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     while (ok) {
       int t;
       if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-      const WorkItem it = decode_item<SUB>(t, p);
+      const WorkItem it = decode_item<SUB, WIN>(t, p);
       for (int i = 0; i < SUB && ok; ++i)
         if (it.nbi(i) > 0) ok = finish(it, i);
     }
@@ -688,9 +707,9 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         return true;
       };
       // O_i (+)= P_i(j) V(j): kParts stages of V, each producing its head-dim slice of O.
-      auto do_PV = [&](bool needed, int j, bool last) -> bool {
+      auto do_PV = [&](bool needed, bool first, bool last) -> bool {
         if (needed) {
-          if (j == 0 && !first_item) {  // the epilogue must have drained O_i
+          if (first && !first_item) {  // the epilogue must have drained O_i
             if (!W.wait_warp(bar(Plan::kOEmpty + i), oe_par)) return false;
             oe_par ^= 1;
           }
@@ -710,7 +729,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBlockN / 16; ++kk) {
             const uint32_t boff = (uint32_t)(kk * 16 * 128) >> 4;
-            const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
             if (C::kPInTmem) {
               ptx::umma_ts_warp(dO, tPi + (uint32_t)(kk * 8), b0 + boff, idPV, acc);
             } else {
@@ -730,20 +749,21 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       while (ok) {
         int t;
         if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-        const WorkItem it = decode_item<SUB>(t, p);
-        const int nb = it.nbi(i);
+        const WorkItem it = decode_item<SUB, WIN>(t, p);
+        const int nb = it.nbi(i), lo = it.loi(i);  // this sub-tile reads tiles [lo, nb)
         if (nb > 0) {
           if (!(ok = W.wait_warp(bar(Plan::kQFull + i), q_par))) break;
           q_par ^= 1;
         }
-        ok = do_S(nb > 0);  // K(0)
-        if (ok && nb == 1) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last use of Q_i
-        for (int j = 0; j < it.nbmax && ok; ++j) {
+        auto mine = [&](int j) { return j >= lo && j < nb; };
+        ok = do_S(mine(it.jlo));  // K(jlo)
+        if (ok && nb > 0 && nb - 1 == it.jlo) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last use of Q_i
+        for (int j = it.jlo; j < it.nbmax && ok; ++j) {
           if (j + 1 < it.nbmax) {
-            ok = do_S(j + 1 < nb);  // K(j+1)
-            if (ok && j + 2 == nb) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last S_i
+            ok = do_S(mine(j + 1));  // K(j+1)
+            if (ok && nb > 0 && j + 2 == nb) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last S_i
           }
-          if (ok) ok = do_PV(j < nb, j, j == nb - 1);  // V(j)
+          if (ok) ok = do_PV(mine(j), j == lo, j == nb - 1);  // V(j)
         }
         if (nb > 0) first_item = false;
       }
@@ -805,7 +825,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
             break;
           }
           if (t < 0) break;
-          const WorkItem it = decode_item<SUB>(t, p);
+          const WorkItem it = decode_item<SUB, WIN>(t, p);
           if (it.nbi(qi) > 0) {
             if (!(ok = W.wait(bar(Plan::kQEmpty + qi), qe_par))) break;
             qe_par ^= 1;
@@ -816,10 +836,11 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
             q_filled = true;
           }
           if (qi != 0) continue;
-          ok = fill(&tmK, 0, it.h, it.b);
-          for (int j = 0; j < it.nbmax && ok; ++j) {
-            if (j + 1 < it.nbmax) ok = fill(&tmK, j + 1, it.h, it.b);
-            if (ok) ok = fill(&tmV, j, it.h, it.b);
+          const int hkv = it.h / p.kv_group;  // grouped-query attention: shared K/V head
+          ok = fill(&tmK, it.jlo, hkv, it.b);
+          for (int j = it.jlo; j < it.nbmax && ok; ++j) {
+            if (j + 1 < it.nbmax) ok = fill(&tmK, j + 1, hkv, it.b);
+            if (ok) ok = fill(&tmV, j, hkv, it.b);
           }
         }
         // Let every load this thread issued land before the CTA exits (normally they were

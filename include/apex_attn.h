@@ -60,6 +60,39 @@ int apex_attn_fwd(const void* q, const void* k, const void* v, void* o, float* l
                   const long long* strides, void* stream);
 
 /*
+ * Extended forward: the operation of apex_attn_fwd plus grouped-query attention and a
+ * causal sliding window, with the arguments in a struct.
+ *   heads_kv     K/V heads; heads_q % heads_kv == 0, query head h reads K/V head
+ *                h / (heads_q / heads_kv). k and v are [B, heads_kv, N, D].
+ *   window_left  -1: no window. >= 0 (causal only): row i sees keys j with
+ *                i - window_left <= j <= i.
+ *   strides      as for apex_attn_fwd (k and v strides refer to their heads_kv heads).
+ * Returns APEX_ATTN_ERR_INVALID_ARGUMENT for heads_q % heads_kv != 0, window_left < -1,
+ * or a window without causal. No counterpart in the reference operator; it covers the
+ * attention call of the reference's nanochat model (flash_attn_func with GQA and
+ * window_size, nanochat_autoresearch/solutions/train.py:690-719).
+ */
+typedef struct apex_attn_fwd_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse; /* nullable */
+  int batch;
+  int heads_q;
+  int heads_kv;
+  int seqlen;
+  int head_dim;
+  int dtype;
+  int causal;
+  int window_left;
+  float sm_scale;
+  long long strides[12];
+} apex_attn_fwd_args;
+
+int apex_attn_fwd_ex(const apex_attn_fwd_args* args, void* stream);
+
+/*
  * Reads and clears the device status word of `device` after synchronising that
  * device. *flags receives the raw bits (1 = a kernel hit its bounded-wait limit,
  * 2 = a copy or MMA still in flight at kernel teardown did not land within the limit,

@@ -47,14 +47,17 @@ def compute_flops(batch: int, nheads: int, seqlen: int, headdim: int, causal: bo
 
 def attention_np(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool = True,
                  sm_scale: float | None = None, chunk: int = 512, dtype=np.float32,
-                 heads: list[int] | None = None):
+                 heads: list[int] | None = None, window_left: int | None = None):
     """softmax(Q K^T * scale + mask) V and its row logsumexp, chunked over query rows.
 
-    q, k, v: [B, H, N, D] arrays (any float dtype; computed in `dtype`).
+    q: [B, H, N, D]; k, v: [B, H_kv, N, D] with H_kv dividing H (query head h reads K/V head
+    h // (H // H_kv): grouped-query attention; H_kv = H is the reference's case).
+    window_left (causal only): row i sees keys i - window_left .. i.
     heads: optional list of flattened (b*H + h) indices to compute (others left zero).
     Returns (o [B,H,N,D] float32, lse [B,H,N] float32).
     """
     B, H, N, D = q.shape
+    group = H // k.shape[1]
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     o = np.zeros((B, H, N, D), dtype=np.float32)
@@ -63,8 +66,8 @@ def attention_np(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool = Tru
     for bh in sel:
         b, h = divmod(int(bh), H)
         qh = q[b, h].astype(dtype, copy=False)
-        kh = k[b, h].astype(dtype, copy=False)
-        vh = v[b, h].astype(dtype, copy=False)
+        kh = k[b, h // group].astype(dtype, copy=False)
+        vh = v[b, h // group].astype(dtype, copy=False)
         for r0 in range(0, N, chunk):
             r1 = min(N, r0 + chunk)
             kmax = r1 if causal else N
@@ -72,7 +75,10 @@ def attention_np(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool = Tru
             if causal:
                 rows = np.arange(r0, r1)[:, None]
                 cols = np.arange(kmax)[None, :]
-                s = np.where(cols > rows, -np.inf, s)
+                hidden = cols > rows
+                if window_left is not None:
+                    hidden |= cols < rows - window_left
+                s = np.where(hidden, -np.inf, s)
             m = s.max(axis=1, keepdims=True)
             e = np.exp(s - m)
             l = e.sum(axis=1, keepdims=True)

@@ -99,3 +99,35 @@ def test_valid_arguments_without_device_report_no_device(lib):
     if torch.cuda.is_available():
         pytest.skip("checks the no-device path")
     assert call(lib) == _lib.ERR_NO_DEVICE
+
+
+def _ex_args(**kw):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, o=FAKE, lse=None, batch=1, heads_q=4, heads_kv=2, seqlen=256,
+             head_dim=64, dtype=0, causal=1, window_left=-1, sm_scale=0.125)
+    a.update(kw)
+    st = (ctypes.c_longlong * 12)(*([4 * 256 * 64, 256 * 64, 64] * 4))
+    return _lib.FwdArgs(strides=st, **a)
+
+
+def test_ex_struct_layout_matches_c_abi():
+    # x86-64 / aarch64 layout of apex_attn_fwd_args: 5 pointers, 8 ints, 1 float, padding
+    # to 8 bytes, then 12 long longs.
+    assert ctypes.sizeof(_lib.FwdArgs) == 176
+    assert _lib.FwdArgs.strides.offset == 80 and _lib.FwdArgs.sm_scale.offset == 72
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(heads_kv=3), _lib.ERR_INVALID_ARGUMENT),            # 4 % 3 != 0
+    (dict(heads_kv=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(window_left=-2), _lib.ERR_INVALID_ARGUMENT),
+    (dict(window_left=16, causal=0), _lib.ERR_INVALID_ARGUMENT),  # windows are causal-only
+    (dict(head_dim=96), _lib.ERR_UNSUPPORTED_HEAD_DIM),
+    (dict(q=None), _lib.ERR_INVALID_ARGUMENT),
+])
+def test_ex_argument_validation(lib, kw, code):
+    a = _ex_args(**kw)
+    assert lib.apex_attn_fwd_ex(ctypes.byref(a), None) == code
+
+
+def test_ex_null_args(lib):
+    assert lib.apex_attn_fwd_ex(None, None) == _lib.ERR_INVALID_ARGUMENT

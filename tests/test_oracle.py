@@ -85,3 +85,29 @@ def test_make_inputs_seeded_and_rounded():
     q, _, _ = make_inputs(1, 1, 8, 64, seed=1, scale_q=8.0)
     assert q.float().abs().max() > 4.0
     assert not math.isnan(q.float().sum().item())
+
+
+def test_oracle_window_and_gqa_against_brute_force():
+    q, k, v = (to_np32(t) for t in make_inputs(1, 4, 40, 16, seed=8))
+    k, v = k[:, :2], v[:, :2]  # 2 K/V heads for 4 query heads
+    for w in (0, 5, 100):
+        o, lse = attention_np(q, k, v, window_left=w, chunk=11)
+        for h in range(4):
+            for i in range(40):
+                js = [j for j in range(40) if i - w <= j <= i]
+                s = np.array([q[0, h, i] @ k[0, h // 2, j] for j in js]) / 4.0
+                e = np.exp(s - s.max())
+                ref = (e[:, None] * v[0, h // 2, js]).sum(0) / e.sum()
+                np.testing.assert_allclose(o[0, h, i], ref, atol=2e-6)
+                assert abs(lse[0, h, i] - (s.max() + math.log(e.sum()))) < 2e-6
+
+
+def test_oracle_window_matches_sdpa_with_explicit_mask():
+    q, k, v = make_inputs(2, 3, 70, 32, seed=9, dtype="float32")
+    w = 9
+    rows = torch.arange(70)[:, None]
+    cols = torch.arange(70)[None, :]
+    allowed = (cols <= rows) & (cols >= rows - w)
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=allowed)
+    o, _ = attention_np(q.numpy(), k.numpy(), v.numpy(), window_left=w)
+    np.testing.assert_allclose(o, ref.numpy(), atol=2e-6)
