@@ -5,6 +5,7 @@ Drop-in for the operator of mls-bench_fused_attention/fused_attention.py:155-193
 from .ops import (custom_attention_forward, device_status, selftest_wait_timeout,
                   supports_head_dim)
 from . import _lib
+from . import torch_op  # registers torch.ops.apex_attn.fwd
 
 __all__ = ["custom_attention_forward", "device_status", "selftest_wait_timeout",
            "supports_head_dim", "library_path", "version"]
