@@ -1,14 +1,17 @@
-"""apex_attn — B200-native (sm_100a) fused causal attention forward.
+"""apex_attn — B200-native (sm_100a) fused causal attention, forward and backward.
 
-Drop-in for the operator of mls-bench_fused_attention/fused_attention.py:155-193.
+Drop-in for the operator of mls-bench_fused_attention/fused_attention.py:155-193; the
+backward and the autograd-enabled ``torch.ops.apex_attn.fwd`` serve training callers such
+as the reference's nanochat model.
 """
-from .ops import (custom_attention_forward, device_status, selftest_wait_timeout,
-                  supports_head_dim)
+from .ops import (custom_attention_backward, custom_attention_forward, device_status,
+                  selftest_wait_timeout, supports_head_dim)
 from . import _lib
-from . import torch_op  # registers torch.ops.apex_attn.fwd
+from . import torch_op  # registers torch.ops.apex_attn.fwd / .bwd
+from .torch_op import attention
 
-__all__ = ["custom_attention_forward", "device_status", "selftest_wait_timeout",
-           "supports_head_dim", "library_path", "version"]
+__all__ = ["attention", "custom_attention_forward", "custom_attention_backward", "device_status",
+           "selftest_wait_timeout", "supports_head_dim", "library_path", "version"]
 
 
 def library_path() -> str:

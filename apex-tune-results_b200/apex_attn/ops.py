@@ -98,6 +98,65 @@ def custom_attention_forward(q, k, v, causal=True, sm_scale=None, return_lse=Fal
     return (o, lse) if return_lse else o
 
 
+def custom_attention_backward(q, k, v, o, lse, dout, causal=True, sm_scale=None, window_left=None):
+    """Gradients (dq, dk, dv) of custom_attention_forward for the upstream gradient `dout`.
+
+    The backward nanochat's attention op calls (``_flash_attn_bwd(q, k, v, out,
+    grad_output, lse, causal=True, window_size_left=w)``,
+    nanochat_autoresearch/solutions/train.py:491,508-519): `o` and `lse` are the forward's
+    output and fp32 logsumexp (``custom_attention_forward(..., return_lse=True)``); the
+    other arguments mean what they mean for the forward. Head dims 64 and 128 (others
+    raise KeyError). dq has q's shape, dk and dv k's (grouped-query heads summed); all in
+    q's dtype. Runs asynchronously on the current CUDA stream; deterministic.
+    """
+    if q.dim() != 4 or k.shape != v.shape or o.shape != q.shape or dout.shape != q.shape:
+        raise ValueError(f"expected q, o, dout [B, H, N, D] and k, v [B, H_kv, N, D], got q "
+                         f"{tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}, o "
+                         f"{tuple(o.shape)}, dout {tuple(dout.shape)}")
+    batch, nheads, seqlen, headdim = q.shape
+    kv_heads = k.shape[1]
+    if (k.shape[0], k.shape[2], k.shape[3]) != (batch, seqlen, headdim) or nheads % kv_heads != 0:
+        raise ValueError(f"k and v must be [B, H_kv, N, D] with H_kv dividing q's heads, got q "
+                         f"{tuple(q.shape)}, k {tuple(k.shape)}")
+    if headdim not in (64, 128):
+        raise KeyError(headdim)
+    if q.dtype not in _DTYPES or any(t.dtype != q.dtype for t in (k, v, o, dout)):
+        raise TypeError("q, k, v, o, dout must share one dtype, float16 or bfloat16")
+    if lse.shape != (batch, nheads, seqlen) or lse.dtype != torch.float32:
+        raise ValueError(f"lse must be float32 [B, H, N], got {lse.dtype} {tuple(lse.shape)}")
+    tensors = (q, k, v, o, dout, lse)
+    if not all(t.is_cuda and t.device == q.device for t in tensors):
+        raise ValueError("all tensors must be CUDA tensors on one device")
+    if window_left is not None and (window_left < 0 or not causal):
+        raise ValueError("window_left must be >= 0 and needs causal=True")
+    q, k, v, o, dout = (_tma_ready(t) for t in (q, k, v, o, dout))
+    lse = lse.contiguous()
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(headdim)
+    dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    dk = torch.empty(k.shape, dtype=q.dtype, device=q.device)
+    dv = torch.empty(k.shape, dtype=q.dtype, device=q.device)
+    if q.numel() == 0:
+        return dq, dk.zero_(), dv.zero_()
+    lib = _lib.load()
+    ws_bytes = int(lib.apex_attn_bwd_workspace_bytes(batch, nheads, seqlen))
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    strides = []
+    for t in (q, k, v, o, dout, dq, dk, dv):
+        strides += _strides(t)
+    args = _lib.BwdArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), o=o.data_ptr(),
+                        dout=dout.data_ptr(), lse=lse.data_ptr(), dq=dq.data_ptr(),
+                        dk=dk.data_ptr(), dv=dv.data_ptr(), batch=batch, heads_q=nheads,
+                        heads_kv=kv_heads, seqlen=seqlen, head_dim=headdim,
+                        dtype=_DTYPES[q.dtype], causal=1 if causal else 0,
+                        window_left=-1 if window_left is None else int(window_left),
+                        sm_scale=float(sm_scale), strides=(ctypes.c_longlong * 24)(*strides))
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = lib.apex_attn_bwd(ctypes.byref(args), workspace.data_ptr(), ws_bytes, stream)
+    _lib.check(rc, "custom_attention_backward")
+    return dq, dk, dv
+
+
 def device_status(device: int | None = None) -> int:
     """Synchronises `device`, returns and clears its status bits (0 = no kernel fault)."""
     if device is None:

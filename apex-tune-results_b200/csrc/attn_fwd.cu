@@ -1,5 +1,6 @@
 // Host side of apex_attn: argument validation, tensor-map encoding, per-device state
-// and kernel dispatch behind the C ABI declared in include/apex_attn.h.
+// and kernel dispatch behind the C ABI declared in include/apex_attn.h (forward and
+// backward).
 //
 // The Python operator custom_attention_forward (mls-bench_fused_attention/
 // fused_attention.py:155-193) did, per call: make q/k/v contiguous, default the scale,
@@ -20,13 +21,14 @@
 #include <mutex>
 
 #include "apex_attn.h"
+#include "attn_bwd_kernel.cuh"
 #include "attn_fwd_kernel.cuh"
 
 namespace {
 
 using apex::AttnParams;
 
-constexpr int kVersion = 200;  // 0.2.0
+constexpr int kVersion = 300;  // 0.3.0
 
 // Build-time tuning knob (overridable with -D for sweeps): exp2 pairs out of every 8 of an
 // unmasked tile that use the FMA-pipe polynomial, per head dim.
@@ -59,6 +61,7 @@ struct DeviceState {
   int num_sms = 0;
   int cc_major = 0, cc_minor = 0;
   unsigned attr_done = 0;  // bit per kernel instantiation
+  unsigned attr_bwd = 0;   // bit per backward kernel instantiation
 };
 
 std::mutex g_mu;
@@ -374,9 +377,177 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   }
 }
 
+// ------------------------------------------------------------------ backward --
+constexpr int kBwdBlock = apex::kBlockM;
+
+long long bwd_padded_rows(int seqlen) { return ((long long)seqlen + kBwdBlock - 1) / kBwdBlock * kBwdBlock; }
+
+// Workspace: lse2 then delta, each fp32 [batch * heads_q][Npad].
+size_t bwd_workspace_bytes(int batch, int heads_q, int seqlen) {
+  if (batch <= 0 || heads_q <= 0 || seqlen <= 0) return 0;
+  return (size_t)2 * (size_t)batch * (size_t)heads_q * (size_t)bwd_padded_rows(seqlen) * sizeof(float);
+}
+
+template <int D, typename T, bool KV, bool WIN>
+int launch_bwd_one(DeviceState& ds, const CUtensorMap& x1, const CUtensorMap& x2, const CUtensorMap& y1,
+                   const CUtensorMap& y2, const apex::BwdParams& p, int grid, cudaStream_t stream) {
+  auto kern = apex::attn_bwd_sm100_kernel<D, T, KV, WIN>;
+  constexpr int smem = apex::BwdSmem<D>::kDynamicBytes;
+  constexpr unsigned bit = 1u << ((D == 128 ? 8 : 0) + (std::is_same<T, __half>::value ? 4 : 0) +
+                                  (KV ? 2 : 0) + (WIN ? 1 : 0));
+  if (!(ds.attr_bwd & bit)) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_LAUNCH;
+    }
+    ds.attr_bwd |= bit;
+  }
+  kern<<<grid, apex::BwdCfg<D>::kThreads, smem, stream>>>(x1, x2, y1, y2, p);
+  if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
+  return APEX_ATTN_OK;
+}
+
+// Prep pass, then the dK/dV pass (K, V stationary) and the dQ pass (Q, dO stationary).
+template <int D, typename T>
+int launch_bwd(DeviceState& ds, const apex_attn_bwd_args& a, const CUtensorMap& mq, const CUtensorMap& mk,
+               const CUtensorMap& mv, const CUtensorMap& mdo, float* lse2, float* delta, cudaStream_t s) {
+  const long long* st = a.strides;
+  const int npad = (int)bwd_padded_rows(a.seqlen);
+  const long long rows = (long long)a.batch * a.heads_q * npad;
+  const long long threads = rows * (D / 8);
+  apex::attn_bwd_prep_kernel<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      static_cast<const T*>(a.o), static_cast<const T*>(a.dout), a.lse, lse2, delta, st[9], st[10], st[11],
+      st[12], st[13], st[14], a.heads_q, a.seqlen, npad, rows);
+  if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
+
+  apex::BwdParams p{};
+  p.lse2 = lse2;
+  p.delta = delta;
+  p.status = ds.status;
+  p.B = a.batch;
+  p.H = a.heads_q;
+  p.Hkv = a.heads_kv;
+  p.N = a.seqlen;
+  p.Npad = npad;
+  p.nblk = npad / kBwdBlock;
+  p.kv_group = a.heads_q / a.heads_kv;
+  p.scale_log2 = a.sm_scale * 1.4426950408889634f;
+  p.out1_scale = a.sm_scale;
+  p.causal = a.causal ? 1 : 0;
+  // A window of seqlen or more hides nothing: run the plain causal kernels (this also keeps
+  // the kernels' window arithmetic far from int overflow).
+  p.window = a.window_left < a.seqlen ? a.window_left : -1;
+  p.timeout_ns = wait_timeout_ns();
+  // L2 groups as in the forward: the streamed tiles of the heads that concurrently running
+  // CTAs walk should stay within ~48 MB of L2.
+  auto set_groups = [&](apex::BwdParams& q, long long heads, double stream_bytes_per_head) {
+    long long g = (long long)(48.0 * 1024 * 1024 / stream_bytes_per_head);
+    g = std::max(1LL, std::min(g, heads));
+    const long long ngroups = (heads + g - 1) / g;
+    q.group_q = (int)(heads / ngroups);
+    q.group_big = (int)(heads % ngroups);
+    q.num_items = (int)(heads * q.nblk);
+  };
+  const bool win = p.window >= 0;
+  int rc;
+  // dK, dV: items over (batch, K/V head, key block); Q and dO of the group stream.
+  apex::BwdParams pk = p;
+  pk.out1 = a.dk;
+  pk.out2 = a.dv;
+  pk.o1_sb = st[18]; pk.o1_sh = st[19]; pk.o1_sn = st[20];
+  pk.o2_sb = st[21]; pk.o2_sh = st[22]; pk.o2_sn = st[23];
+  set_groups(pk, (long long)a.batch * a.heads_kv, 2.0 * npad * D * 2.0 * pk.kv_group);
+  pk.work_counter = ds.status + kCounterBase + (int)(g_counter_seq.fetch_add(1) % kCounterSlots);
+  if (cudaMemsetAsync(pk.work_counter, 0, sizeof(int), s) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_CUDA;
+  }
+  const int grid_kv = std::min(pk.num_items, ds.num_sms);
+  rc = win ? launch_bwd_one<D, T, true, true>(ds, mk, mv, mq, mdo, pk, grid_kv, s)
+           : launch_bwd_one<D, T, true, false>(ds, mk, mv, mq, mdo, pk, grid_kv, s);
+  if (rc != APEX_ATTN_OK) return rc;
+  // dQ: items over (batch, query head, query block); K and V stream.
+  apex::BwdParams pq = p;
+  pq.out1 = a.dq;
+  pq.o1_sb = st[15]; pq.o1_sh = st[16]; pq.o1_sn = st[17];
+  set_groups(pq, (long long)a.batch * a.heads_q, 2.0 * npad * D * 2.0 / pq.kv_group);
+  pq.work_counter = ds.status + kCounterBase + (int)(g_counter_seq.fetch_add(1) % kCounterSlots);
+  if (cudaMemsetAsync(pq.work_counter, 0, sizeof(int), s) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_CUDA;
+  }
+  const int grid_q = std::min(pq.num_items, ds.num_sms);
+  return win ? launch_bwd_one<D, T, false, true>(ds, mq, mdo, mk, mv, pq, grid_q, s)
+             : launch_bwd_one<D, T, false, false>(ds, mq, mdo, mk, mv, pq, grid_q, s);
+}
+
+int backward(const apex_attn_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+  // ---- argument validation (no CUDA calls) ----
+  if (!a) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv || !workspace)
+    return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->batch <= 0 || a->heads_q <= 0 || a->seqlen <= 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->heads_kv <= 0 || a->heads_q % a->heads_kv != 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->window_left < -1 || (a->window_left >= 0 && !a->causal)) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->head_dim != 64 && a->head_dim != 128) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
+  if (a->dtype != APEX_ATTN_BF16 && a->dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
+  if (!std::isfinite(a->sm_scale) || !(a->sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
+  const long long npad = bwd_padded_rows(a->seqlen);
+  const long long items = (long long)a->batch * a->heads_q * (npad / kBwdBlock);
+  if (items > 0x7fffffffLL || a->seqlen > (1 << 30) || (long long)a->batch * a->heads_q * npad > (1LL << 40))
+    return APEX_ATTN_ERR_TOO_LARGE;
+  for (int i = 0; i < 24; ++i)
+    if (a->strides[i] < 0 || (a->strides[i] & 7) != 0 || a->strides[i] >= (1LL << 38)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  for (int t = 0; t < 8; ++t)
+    if (a->strides[3 * t + 2] < a->head_dim) return APEX_ATTN_ERR_BAD_LAYOUT;
+  const void* ptrs[8] = {a->q, a->k, a->v, a->o, a->dout, a->dq, a->dk, a->dv};
+  for (const void* ptr : ptrs)
+    if (!aligned16(ptr)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  if ((reinterpret_cast<uintptr_t>(a->lse) & 3u) || !aligned16(workspace)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  if (workspace_bytes < bwd_workspace_bytes(a->batch, a->heads_q, a->seqlen)) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+
+  // ---- device ----
+  const int dev = device_of(a->q);
+  if (dev < 0) return APEX_ATTN_ERR_NO_DEVICE;
+  for (const void* ptr : ptrs)
+    if (device_of(ptr) != dev) return APEX_ATTN_ERR_NO_DEVICE;
+  if (device_of(a->lse) != dev || device_of(workspace) != dev) return APEX_ATTN_ERR_NO_DEVICE;
+  DeviceGuard guard(dev);
+  DeviceState* ds = nullptr;
+  int rc = init_device(dev, &ds);
+  if (rc != APEX_ATTN_OK) return rc;
+
+  const long long* st = a->strides;
+  const int B = a->batch, H = a->heads_q, HKV = a->heads_kv, N = a->seqlen, D = a->head_dim;
+  CUtensorMap mq, mk, mv, mdo;
+  if ((rc = encode_map(&mq, a->q, a->dtype, B, H, N, D, st[0], st[1], st[2])) ||
+      (rc = encode_map(&mk, a->k, a->dtype, B, HKV, N, D, st[3], st[4], st[5])) ||
+      (rc = encode_map(&mv, a->v, a->dtype, B, HKV, N, D, st[6], st[7], st[8])) ||
+      (rc = encode_map(&mdo, a->dout, a->dtype, B, H, N, D, st[12], st[13], st[14])))
+    return rc;
+  float* lse2 = static_cast<float*>(workspace);
+  float* delta = lse2 + (size_t)B * H * npad;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf16 = a->dtype == APEX_ATTN_BF16;
+  if (D == 64)
+    return bf16 ? launch_bwd<64, __nv_bfloat16>(*ds, *a, mq, mk, mv, mdo, lse2, delta, s)
+                : launch_bwd<64, __half>(*ds, *a, mq, mk, mv, mdo, lse2, delta, s);
+  return bf16 ? launch_bwd<128, __nv_bfloat16>(*ds, *a, mq, mk, mv, mdo, lse2, delta, s)
+              : launch_bwd<128, __half>(*ds, *a, mq, mk, mv, mdo, lse2, delta, s);
+}
+
 }  // namespace
 
 extern "C" {
+
+size_t apex_attn_bwd_workspace_bytes(int batch, int heads_q, int seqlen) {
+  return bwd_workspace_bytes(batch, heads_q, seqlen);
+}
+
+int apex_attn_bwd(const apex_attn_bwd_args* args, void* workspace, size_t workspace_bytes, void* stream) {
+  return backward(args, workspace, workspace_bytes, stream);
+}
 
 int apex_attn_version(void) { return kVersion; }
 

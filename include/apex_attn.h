@@ -1,10 +1,10 @@
 /*
- * apex_attn — C ABI of the B200 (sm_100a) fused attention forward.
+ * apex_attn — C ABI of the B200 (sm_100a) fused attention forward and backward.
  *
  * This header is the drop-in boundary for the operator
  *   custom_attention_forward(q, k, v, causal=True, sm_scale=None) -> o
  * of mls-bench_fused_attention/fused_attention.py:155-193 (identical copy at
- * submission.py:179-217). The Python host module `apex_attn` binds it with ctypes;
+ * submission.py:179-217); apex_attn_bwd adds the backward that training callers need. The Python host module `apex_attn` binds it with ctypes;
  * any other FFI binds the same symbols.
  *
  * Conventions: all pointers are device pointers on one CUDA device, tensors are
@@ -16,6 +16,8 @@
  */
 #ifndef APEX_ATTN_H_
 #define APEX_ATTN_H_
+
+#include <stddef.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -136,6 +138,55 @@ int apex_attn_selftest_wait_timeout(int timeout_us, void* stream);
 int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
                           int batch, int heads, int seqlen, int head_dim, int dtype, int causal,
                           float sm_scale, const long long* strides, void* stream);
+
+/*
+ * Backward of the attention computed by apex_attn_fwd / apex_attn_fwd_ex:
+ *   dq = d(sum o * dout)/dq, dk, dv likewise, for the same causal / window_left / grouped-
+ *   query settings. Inputs: q, k, v, the forward output o, the upstream gradient dout (all
+ *   of the input dtype) and the forward's fp32 natural-log logsumexp lse (contiguous
+ *   [B, heads_q, N], as apex_attn_fwd writes it). Outputs dq [B, heads_q, N, D] and dk, dv
+ *   [B, heads_kv, N, D] in the input dtype; grouped-query heads sum into their K/V head.
+ *
+ * strides: 24 values, element strides (batch, head, seq) of q, k, v, o, dout, dq, dk, dv in
+ * that order; the rules of apex_attn_fwd apply to each (unit head-dim stride, multiples of
+ * 8 elements, 16-byte aligned pointers), so [B, N, H, D] views need no copy.
+ * head_dim: 64 or 128 (else APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM).
+ * workspace: device memory of at least apex_attn_bwd_workspace_bytes(batch, heads_q,
+ * seqlen) bytes, 16-byte aligned, on the same device; used only during the call (it holds
+ * two fp32 values per query row). Smaller: APEX_ATTN_ERR_INVALID_ARGUMENT.
+ * Asynchronous on `stream`; results are deterministic (no atomics).
+ *
+ * Replaces: _flash_attn_bwd(q, k, v, out, grad_output, lse, causal=True,
+ * window_size_left=w), the backward that nanochat's attention custom op calls
+ * (nanochat_autoresearch/solutions/train.py:491,508-519).
+ */
+typedef struct apex_attn_bwd_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  const float* lse;
+  void* dq;
+  void* dk;
+  void* dv;
+  int batch;
+  int heads_q;
+  int heads_kv;
+  int seqlen;
+  int head_dim;
+  int dtype;
+  int causal;
+  int window_left;
+  float sm_scale;
+  long long strides[24];
+} apex_attn_bwd_args;
+
+/* Bytes of workspace apex_attn_bwd needs (0 for non-positive sizes). */
+size_t apex_attn_bwd_workspace_bytes(int batch, int heads_q, int seqlen);
+
+int apex_attn_bwd(const apex_attn_bwd_args* args, void* workspace, size_t workspace_bytes,
+                  void* stream);
 
 /* Human-readable text for a status code. Replaces the exception text the reference
  * harness prints on failure (submission.py:299-306). */

@@ -18,6 +18,13 @@ What it restates
   the same ``F.scaled_dot_product_attention`` call (submission.py:227-232; its
   ``sdp_kernel`` context only selects CUDA backends, so it is dropped on CPU).
   This is what the CPU baseline times.
+* ``attention_bwd_np`` — the gradients dQ, dK, dV of the same quantity for an upstream
+  gradient dO: the backward that nanochat's Blackwell attention op calls
+  (``_flash_attn_bwd(q, k, v, out, grad_output, lse, causal=True, window_size_left=...)``,
+  nanochat_autoresearch/solutions/train.py:491,508-519). It is the textbook derivative of
+  softmax(S) V, written out (P = softmax(S), dV = P^T dO, dP = dO V^T,
+  dS = P * (dP - rowsum(dO * O)), dQ = scale dS K, dK = scale dS^T Q; grouped-query heads
+  sum into their shared K/V head).
 * ``compute_flops`` — submission.py:235-240 (4*B*N^2*H*d, halved when causal).
 * ``make_inputs`` — the harness's seeded ``randn`` inputs (submission.py:278-287), drawn
   on the CPU generator in fp32 and rounded to the kernel dtype, so CPU and GPU see the
@@ -26,7 +33,9 @@ What it restates
 Pinning: tests/golden/ holds vectors produced by the reference's own code in the build
 container (the harness ``reference_attention`` and the reference Triton kernel
 ``_attn_fwd_plain`` run under the Triton CPU interpreter); tests/test_oracle.py checks
-this module against them. See tests/golden/make_golden.py.
+this module against them. See tests/golden/make_golden.py. The backward is pinned to
+torch autograd through the same harness oracle (``bwd_*.npz``, written by
+tests/golden/make_golden_bwd.py).
 """
 from __future__ import annotations
 
@@ -85,6 +94,68 @@ def attention_np(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool = Tru
             o[b, h, r0:r1] = (e @ vh[:kmax]) / l
             lse[b, h, r0:r1] = (m + np.log(l))[:, 0]
     return o, lse
+
+
+def attention_bwd_np(q: np.ndarray, k: np.ndarray, v: np.ndarray, do: np.ndarray,
+                     causal: bool = True, sm_scale: float | None = None,
+                     window_left: int | None = None, dtype=np.float64, heads: list[int] | None = None):
+    """Gradients of softmax(Q K^T * scale + mask) V with respect to q, k and v.
+
+    q, do: [B, H, N, D]; k, v: [B, H_kv, N, D] (grouped-query heads as in attention_np).
+    The forward's O and logsumexp are recomputed here in `dtype` (float64 by default), so
+    the result is the exact gradient of the masked attention, not of a rounded O.
+    heads: optional flattened (b*H + h) query-head indices to include (others contribute
+    nothing; their dq rows stay zero).
+    Returns (dq [B,H,N,D], dk [B,H_kv,N,D], dv [B,H_kv,N,D]) as float32.
+    """
+    B, H, N, D = q.shape
+    hkv = k.shape[1]
+    group = H // hkv
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    dq = np.zeros((B, H, N, D), dtype=np.float64)
+    dk = np.zeros((B, hkv, N, D), dtype=np.float64)
+    dv = np.zeros((B, hkv, N, D), dtype=np.float64)
+    rows = np.arange(N)[:, None]
+    cols = np.arange(N)[None, :]
+    hidden = np.zeros((N, N), dtype=bool)
+    if causal:
+        hidden = cols > rows
+        if window_left is not None:
+            hidden |= cols < rows - window_left
+    sel = range(B * H) if heads is None else heads
+    for bh in sel:
+        b, h = divmod(int(bh), H)
+        g = h // group
+        qh = q[b, h].astype(dtype)
+        kh = k[b, g].astype(dtype)
+        vh = v[b, g].astype(dtype)
+        doh = do[b, h].astype(dtype)
+        s = np.where(hidden, -np.inf, (qh @ kh.T) * sm_scale)
+        m = s.max(axis=1, keepdims=True)
+        e = np.exp(s - m)
+        p = e / e.sum(axis=1, keepdims=True)
+        o = p @ vh
+        dp = doh @ vh.T
+        delta = (doh * o).sum(axis=1, keepdims=True)  # = rowsum(P * dP)
+        ds = p * (dp - delta)
+        dq[b, h] = (ds @ kh) * sm_scale
+        dk[b, g] += (ds.T @ qh) * sm_scale
+        dv[b, g] += p.T @ doh
+    return dq.astype(np.float32), dk.astype(np.float32), dv.astype(np.float32)
+
+
+def grad_close(actual: np.ndarray, expected: np.ndarray, atol: float = 1e-2,
+               rtol: float = 2.0 ** -7) -> tuple[bool, float]:
+    """Tolerance of the 16-bit backward: |a - e| <= atol + rtol |e| elementwise.
+
+    The kernel rounds P and dS to 16 bits for the tensor cores and the gradients to the
+    output dtype; the bf16 rounding of a gradient of magnitude ~4 alone is 2^-7. Returns
+    (ok, worst ratio of |a - e| to the bound).
+    """
+    bound = atol + rtol * np.abs(expected)
+    ratio = float((np.abs(actual.astype(np.float64) - expected) / bound).max()) if expected.size else 0.0
+    return ratio <= 1.0, ratio
 
 
 def reference_attention_cpu(q, k, v, causal: bool = True, sm_scale: float | None = None):

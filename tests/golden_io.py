@@ -29,4 +29,23 @@ def load_case(path: str) -> dict:
 
 
 def cases() -> list[str]:
-    return sorted(glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+    """Forward fixtures (tests/golden/make_golden.py)."""
+    return sorted(p for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
+                  if not os.path.basename(p).startswith("bwd_"))
+
+
+def bwd_cases() -> list[str]:
+    """Backward fixtures (tests/golden/make_golden_bwd.py)."""
+    return sorted(glob.glob(os.path.join(GOLDEN_DIR, "bwd_*.npz")))
+
+
+def load_bwd_case(path: str) -> dict:
+    z = np.load(path, allow_pickle=False)
+    out = {"name": os.path.basename(path)[:-4]}
+    for key in ("q", "k", "v", "dout"):
+        out[key] = bf16_bits_to_f32(z[key]).astype(np.float32)
+    for key in ("dq", "dk", "dv"):
+        out[key] = z[key]
+    B, H, HKV, N, D, causal, win = (int(x) for x in z["meta"])
+    out.update(B=B, H=H, HKV=HKV, N=N, D=D, causal=bool(causal), window=None if win < 0 else win)
+    return out

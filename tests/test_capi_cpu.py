@@ -131,3 +131,77 @@ def test_ex_argument_validation(lib, kw, code):
 
 def test_ex_null_args(lib):
     assert lib.apex_attn_fwd_ex(None, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+# ---------------------------------------------------------------- backward --
+def _bwd_args(**kw):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, o=FAKE, dout=FAKE, lse=FAKE, dq=FAKE, dk=FAKE, dv=FAKE,
+             batch=1, heads_q=4, heads_kv=2, seqlen=256, head_dim=64, dtype=0, causal=1,
+             window_left=-1, sm_scale=0.125)
+    strides = kw.pop("strides", [4 * 256 * 64, 256 * 64, 64] * 8)
+    a.update(kw)
+    return _lib.BwdArgs(strides=(ctypes.c_longlong * 24)(*strides), **a)
+
+
+def _c_layout(struct: str, fields: list[str]) -> list[int]:
+    """sizeof and offsetof of `struct` as the C compiler lays it out from the header."""
+    import subprocess
+    import tempfile
+    src = "#include <stdio.h>\n#include <stddef.h>\n#include \"apex_attn.h\"\nint main(void){"
+    src += f'printf("%zu", sizeof({struct}));'
+    for f in fields:
+        src += f'printf(" %zu", offsetof({struct}, {f}));'
+    src += "return 0;}\n"
+    with tempfile.TemporaryDirectory() as d:
+        c, exe = os.path.join(d, "l.c"), os.path.join(d, "l")
+        open(c, "w").write(src)
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        return [int(x) for x in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
+
+
+@pytest.mark.parametrize("cls,struct", [(_lib.FwdArgs, "apex_attn_fwd_args"),
+                                        (_lib.BwdArgs, "apex_attn_bwd_args")])
+def test_ctypes_structs_match_c_compiler_layout(cls, struct):
+    import shutil
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    names = [f[0] for f in cls._fields_]
+    expect = _c_layout(struct, names)
+    assert [ctypes.sizeof(cls)] + [getattr(cls, n).offset for n in names] == expect
+
+
+def test_bwd_workspace_bytes(lib):
+    assert lib.apex_attn_bwd_workspace_bytes(2, 3, 130) == 2 * 2 * 3 * 256 * 4
+    assert lib.apex_attn_bwd_workspace_bytes(1, 1, 128) == 2 * 128 * 4
+    assert lib.apex_attn_bwd_workspace_bytes(0, 3, 130) == 0
+    assert lib.apex_attn_bwd_workspace_bytes(1, 1, -1) == 0
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(dout=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(lse=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(dq=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(heads_kv=3), _lib.ERR_INVALID_ARGUMENT),
+    (dict(window_left=8, causal=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(seqlen=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(head_dim=256), _lib.ERR_UNSUPPORTED_HEAD_DIM),
+    (dict(head_dim=96), _lib.ERR_UNSUPPORTED_HEAD_DIM),
+    (dict(dtype=5), _lib.ERR_UNSUPPORTED_DTYPE),
+    (dict(sm_scale=0.0), _lib.ERR_BAD_SCALE),
+    (dict(strides=[4 * 256 * 64, 256 * 64, 64] * 7 + [4 * 256 * 64, 256 * 64, 36]), _lib.ERR_BAD_LAYOUT),
+    (dict(strides=[4 * 256 * 64, 256 * 64, 32] * 8), _lib.ERR_BAD_LAYOUT),
+    (dict(dv=FAKE + 8), _lib.ERR_BAD_LAYOUT),
+    (dict(lse=FAKE + 2), _lib.ERR_BAD_LAYOUT),
+])
+def test_bwd_argument_validation(lib, kw, code):
+    a = _bwd_args(**kw)
+    assert lib.apex_attn_bwd(ctypes.byref(a), FAKE, 1 << 20, None) == code
+
+
+def test_bwd_workspace_checks(lib):
+    a = _bwd_args()
+    need = lib.apex_attn_bwd_workspace_bytes(1, 4, 256)
+    assert lib.apex_attn_bwd(ctypes.byref(a), None, need, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.apex_attn_bwd(ctypes.byref(a), FAKE, need - 4, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.apex_attn_bwd(ctypes.byref(a), FAKE + 4, need, None) == _lib.ERR_BAD_LAYOUT
+    assert lib.apex_attn_bwd(None, FAKE, need, None) == _lib.ERR_INVALID_ARGUMENT

@@ -111,3 +111,56 @@ def test_oracle_window_matches_sdpa_with_explicit_mask():
     ref = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=allowed)
     o, _ = attention_np(q.numpy(), k.numpy(), v.numpy(), window_left=w)
     np.testing.assert_allclose(o, ref.numpy(), atol=2e-6)
+
+
+# ---------------------------------------------------------------- backward --
+from golden_io import bwd_cases, load_bwd_case  # noqa: E402
+from oracle.attention_oracle import attention_bwd_np, grad_close  # noqa: E402
+
+BWD_CASES = bwd_cases()
+
+
+def test_backward_golden_fixtures_present():
+    assert len(BWD_CASES) >= 5
+
+
+@pytest.mark.parametrize("path", BWD_CASES, ids=lambda p: os.path.basename(p)[:-4])
+def test_backward_oracle_matches_autograd_golden(path):
+    c = load_bwd_case(path)
+    dq, dk, dv = attention_bwd_np(c["q"], c["k"], c["v"], c["dout"], causal=c["causal"],
+                                  window_left=c["window"])
+    for got, key in ((dq, "dq"), (dk, "dk"), (dv, "dv")):
+        np.testing.assert_allclose(got, c[key], atol=2e-5, rtol=0, err_msg=key)
+
+
+def test_backward_oracle_finite_differences():
+    """Directional derivative of sum(O * dO) along a random direction vs the oracle."""
+    rng = np.random.default_rng(3)
+    q, k, v, do = (rng.standard_normal((1, 2, 24, 8)) for _ in range(4))
+    k, v = k[:, :1], v[:, :1]  # grouped-query: 2 query heads share one K/V head
+    for causal, win in ((True, None), (False, None), (True, 5)):
+        def f(q_, k_, v_):  # float64 forward (attention_np returns float32)
+            n = q_.shape[2]
+            i, j = np.arange(n)[:, None], np.arange(n)[None, :]
+            hidden = (j > i) | ((j < i - win) if win is not None else False) if causal else j < 0
+            total = 0.0
+            for h in range(q_.shape[1]):
+                s = np.where(hidden, -np.inf, q_[0, h] @ k_[0, 0].T / math.sqrt(q_.shape[3]))
+                e = np.exp(s - s.max(axis=1, keepdims=True))
+                total += float(((e / e.sum(axis=1, keepdims=True)) @ v_[0, 0] * do[0, h]).sum())
+            return total
+        dq, dk, dv = attention_bwd_np(q, k, v, do, causal=causal, window_left=win)
+        dirs = [rng.standard_normal(t.shape) for t in (q, k, v)]
+        eps = 1e-4
+        plus = f(q + eps * dirs[0], k + eps * dirs[1], v + eps * dirs[2])
+        minus = f(q - eps * dirs[0], k - eps * dirs[1], v - eps * dirs[2])
+        numeric = (plus - minus) / (2 * eps)
+        analytic = float((dq * dirs[0]).sum() + (dk * dirs[1]).sum() + (dv * dirs[2]).sum())
+        assert abs(numeric - analytic) < 1e-3 * max(1.0, abs(analytic)), (causal, win)
+
+
+def test_grad_close_bound():
+    e = np.array([0.0, 1.0, -4.0])
+    assert grad_close(e + np.array([0.009, 0.0, 0.0]), e)[0]
+    assert not grad_close(e + np.array([0.011, 0.0, 0.0]), e)[0]
+    assert grad_close(e + np.array([0.0, 0.0, 0.04]), e)[0]  # 1e-2 + 4 * 2^-7 = 0.041
