@@ -26,17 +26,41 @@
 // atomics from the dK/dV pass, trading 40% more tensor work for deterministic results and
 // no fp32 dQ scratch.
 //
-// In both passes P and dS are written back into the TMEM columns of the scores they came
-// from, packed as 16-bit pairs, and read from there as the A operand of the accumulating
-// MMAs, so the only shared-memory traffic is the TMA tiles.
+// TMEM and scheduling (both passes, 128 x 128 tiles, one CTA per SM):
+//   T1 [0, 128)     scores S^T | S (fp32). The elementwise warps read them into registers
+//                   and release T1 at once, so the next step's score GEMM overlaps the
+//                   exponentials of this one.
+//   T2 [128, 256)   dP^T | dP (fp32); after the elementwise pass it holds the 16-bit
+//                   operands of the accumulating GEMMs, packed two per column: warpgroup h
+//                   writes P_h (KV pass) and dS_h into its own 64 columns.
+//   Acc1, Acc2      dK and dV (KV pass) or dQ (Q pass), fp32, for the whole item.
+//   X (Q pass)      Q and dO of the item, copied from shared memory into the 128 free
+//                   columns, so the score GEMMs read A from TMEM and only B (K, V tiles)
+//                   from shared memory.
+// The MMA warp runs a software pipeline: G1(s+1) (scores) is issued once the elementwise
+// warps hold S(s), then the accumulating GEMMs of step s, then G2(s+1) (dP), whose
+// target T2 becomes free when those complete. A 128 x 128 x 16 MMA whose A and B both come
+// from shared memory reads 8 KB, the shared-memory bandwidth of its 64 tensor cycles, so
+// every GEMM here is at least 128 wide in N.
 //
-// Warp roles (320 threads): warps 0-7 elementwise (warpgroup h handles columns
-// [64h, 64h + 64) of the 128 x 128 tile, a half with its own barriers, so the two halves
-// pipeline against each other's MMAs; thread = TMEM lane = row) and the per-item epilogue;
-// warp 8 issues every MMA (and owns TMEM); warp 9 schedules items and issues TMA.
+// Warp roles (384 threads): warps 0-7 elementwise (warpgroup h handles columns
+// [64h, 64h + 64) of the 128 x 128 tile; thread = TMEM lane = row) and the per-item
+// epilogue; warp 8 issues every MMA (and owns TMEM); warp 9 schedules items and issues TMA;
+// warps 10-11 only give their registers to the elementwise warpgroups.
 #pragma once
 
 #include "attn_fwd_kernel.cuh"
+
+#ifndef APEX_BWD_SPLIT_DP_KV
+#define APEX_BWD_SPLIT_DP_KV 1
+#endif
+// Of every 8 pairs of exponentials in an unmasked tile, how many the elementwise warps take
+// from the FMA-pipe polynomial (exp2_poly_pair) instead of MUFU ex2. Both warpgroups run
+// their exponentials at the same time, which is MUFU-bound (16 per clock per SM) while
+// the FMA pipe idles.
+#ifndef APEX_BWD_EMU
+#define APEX_BWD_EMU 0
+#endif
 
 namespace apex {
 
@@ -45,8 +69,8 @@ struct BwdParams {
   void* out2;            // dV (KV pass)
   long long o1_sb, o1_sh, o1_sn;
   long long o2_sb, o2_sh, o2_sn;
-  const float* lse2;     // workspace [B * H][Npad]: lse * log2(e), +inf on padding rows
-  const float* delta;    // workspace [B * H][Npad]: rowsum(dO * O), 0 on padding rows
+  const float* nlse2;    // workspace [B * H][Npad]: -lse * log2(e), -inf on padding rows
+  const float* ndelta;   // workspace [B * H][Npad]: -rowsum(dO * O), 0 on padding rows
   int* status;
   int* work_counter;
   int B, H, Hkv, N, Npad;
@@ -64,16 +88,30 @@ struct BwdParams {
 template <int D>
 struct BwdCfg {
   static_assert(D == 64 || D == 128, "backward head dims 64, 128");
-  static constexpr int kNS = D == 64 ? 8 : 4;  // streaming ring stages (one 128-row tile each)
-  static constexpr int kThreads = 320;
+  // Streaming ring stages (one 128-row tile each). A stage frees when the accumulating GEMMs
+  // of its step finish and takes ~1300 cycles to refill from L2, so the ring holds about
+  // two and a half steps (two tiles per step).
+  static constexpr int kNS = D == 64 ? 10 : 5;
+  // 12 warps: 8 elementwise, MMA, producer, 2 idle. Registers are granted per warpgroup,
+  // so the launch budget is 384 x 168; setmaxnreg moves it to the elementwise warpgroups
+  // (the split must not exceed the launch allocation, or setmaxnreg.inc would never return).
+  static constexpr int kThreads = 384;
   static constexpr int kWarpMma = 8;
   static constexpr int kWarpProd = 9;
-  // TMEM columns: T1 scores, T2 dP, Acc1 dK | dQ, Acc2 dV.
+  static constexpr int kRegsElementwise = 224;
+  static constexpr int kRegsOther = 56;
+  static constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
+  static_assert(128 * (2 * kRegsElementwise + kRegsOther) <= kThreads * kLaunchRegs,
+                "setmaxnreg split exceeds the launch register allocation");
+  // TMEM columns: T1 scores, T2 dP (then packed P / dS), Acc1 dK | dQ, Acc2 dV (KV pass),
+  // XQ / XdO the item's Q and dO as 16-bit pairs (Q pass).
   static constexpr int kT1 = 0;
   static constexpr int kT2 = 128;
   static constexpr int kAcc1 = 256;
   static constexpr int kAcc2 = 256 + D;
-  static_assert(kAcc2 + D <= 512, "TMEM plan overflows 512 columns");
+  static constexpr int kXQ = 256 + D;
+  static constexpr int kXdO = kXQ + D / 2;
+  static_assert(kAcc2 + D <= 512 && kXdO + D / 2 <= 512, "TMEM plan overflows 512 columns");
 };
 
 template <int D>
@@ -85,20 +123,25 @@ struct BwdSmem {
   static constexpr int kX1 = 0;
   static constexpr int kX2 = kX1 + kTileBytes;
   static constexpr int kRing = kX2 + kTileBytes;
-  static constexpr int kStats = kRing + NS * kTileBytes;  // float [NS][256]: lse2[128], delta[128]
+  // KV pass: per-column statistics of the step's query tile, double-buffered:
+  // float [2][256] = -lse2[128], -delta[128].
+  static constexpr int kStats = kRing + NS * kTileBytes;
   static constexpr int kStatsBytes = 1024;
-  static constexpr int kBars = kStats + NS * kStatsBytes;
+  static constexpr int kBars = kStats + 2 * kStatsBytes;
   static constexpr int kRingFull = 0;
   static constexpr int kRingEmpty = NS;
-  static constexpr int kXFull = 2 * NS;
-  static constexpr int kXEmpty = kXFull + 1;
-  // Per column half h of the 128 x 128 tile (two slots each):
-  static constexpr int kT1Full = kXEmpty + 1;  // [2] scores of half h in TMEM
-  static constexpr int kT2Full = kT1Full + 2;  // [2] dP of half h in TMEM
-  static constexpr int kPFull = kT2Full + 2;   // [2] P of half h packed in TMEM (KV pass)
-  static constexpr int kDSFull = kPFull + 2;   // [2] dS of half h packed in TMEM
-  static constexpr int kTFree = kDSFull + 2;   // [2] accumulating MMAs of half h done
-  static constexpr int kAccFull = kTFree + 2;
+  static constexpr int kXFull = 2 * NS;         // X tiles of the item landed in shared memory
+  static constexpr int kXEmpty = kXFull + 1;    // shared-memory X may be refilled
+  static constexpr int kXTFull = kXEmpty + 1;   // Q pass: X copied into TMEM
+  static constexpr int kXTFree = kXTFull + 1;   // Q pass: last MMA reading TMEM X done
+  static constexpr int kT1Full = kXTFree + 1;
+  static constexpr int kT1Free = kT1Full + 1;   // elementwise warps hold S in registers
+  static constexpr int kT2Full = kT1Free + 1;   // [2] dP of column half h
+  static constexpr int kT2Free = kT2Full + 2;   // [2] accumulating GEMMs of half h done
+  static constexpr int kPdSFull = kT2Free + 2;  // [2] P_h / dS_h packed in T2
+  static constexpr int kStatsFull = kPdSFull + 2;    // [2]
+  static constexpr int kStatsEmpty = kStatsFull + 2;  // [2]
+  static constexpr int kAccFull = kStatsEmpty + 2;
   static constexpr int kAccEmpty = kAccFull + 1;
   static constexpr int kDrain = kAccEmpty + 1;
   static constexpr int kItemFull = kDrain + 1;
@@ -107,8 +150,11 @@ struct BwdSmem {
   static constexpr int kItems = kBars + kNumBars * 8;
   static constexpr int kMisc = kItems + kItemRing * 4;  // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16;
-  static constexpr int kDynamicBytes = kBytes + 1024;
-  static_assert(kDynamicBytes <= 232448, "shared-memory plan exceeds 227 KB");
+  static constexpr int kMaxDynamic = 232448;  // 227 KB per CTA on sm_100
+  // 1 KB of alignment slack when it fits; otherwise the kernel relies on the dynamic shared
+  // memory base being 1 KB aligned and checks it (as the forward does).
+  static constexpr int kDynamicBytes = kBytes + 1024 <= kMaxDynamic ? kBytes + 1024 : kBytes;
+  static_assert(kBytes <= kMaxDynamic, "shared-memory plan exceeds 227 KB");
 };
 
 // One work item: the stationary 128-row block `blk` of head `hx` (K/V head in the KV pass,
@@ -159,15 +205,16 @@ __device__ __forceinline__ BwdItem decode_bwd(int t, const BwdParams& p) {
   return it;
 }
 
-// delta[bh][i] = sum_d dO[b,h,i,d] O[b,h,i,d] (fp32) and lse2[bh][i] = lse[bh][i] log2(e),
-// for i < Npad (padding rows: delta 0, lse2 +inf). kTpr = D / 8 threads per row, each
-// reading one 16-byte vector of O and of dO.
+// ndelta[bh][i] = -sum_d dO[b,h,i,d] O[b,h,i,d] (fp32) and nlse2[bh][i] = -lse[bh][i] log2(e)
+// for i < Npad (padding rows: ndelta 0, nlse2 -inf), stored negated so the elementwise
+// warps add them with one packed instruction. kTpr = D / 8 threads per row, each reading
+// one 16-byte vector of O and of dO.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const T* __restrict__ o,
                                                             const T* __restrict__ dout,
                                                             const float* __restrict__ lse,
-                                                            float* __restrict__ lse2,
-                                                            float* __restrict__ delta, long long o_sb,
+                                                            float* __restrict__ nlse2,
+                                                            float* __restrict__ ndelta, long long o_sb,
                                                             long long o_sh, long long o_sn,
                                                             long long d_sb, long long d_sh,
                                                             long long d_sn, int H, int N, int Npad,
@@ -192,8 +239,8 @@ __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const T* __restrict_
 #pragma unroll
   for (int w = kTpr / 2; w > 0; w >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, w);
   if (in_range && sub == 0) {
-    delta[row] = acc;
-    lse2[row] = i < N ? lse[bh * N + i] * 1.4426950408889634f : INFINITY;
+    ndelta[row] = -acc;
+    nlse2[row] = i < N ? lse[bh * N + i] * -1.4426950408889634f : -INFINITY;
   }
 }
 
@@ -207,8 +254,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
   using C = BwdCfg<D>;
   using Plan = BwdSmem<D>;
   constexpr int NS = C::kNS;
+  constexpr int kEmu = APEX_BWD_EMU;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  if (Plan::kDynamicBytes == Plan::kBytes && (raw_addr & 1023u) != 0) {
+    // The plan needs the whole 227 KB and the base is not 1 KB aligned: report, do nothing.
+    if (threadIdx.x == 0) atomicOr(p.status, kStatusSmemAlign);
+    return;
+  }
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
   const uint32_t sbase = raw_addr + pad;
   uint8_t* smem = smem_raw + pad;
@@ -226,13 +279,17 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       ptx::mbar_init(bar(Plan::kRingEmpty + s), 1);
     }
     ptx::mbar_init(bar(Plan::kXFull), 1);
-    ptx::mbar_init(bar(Plan::kXEmpty), 1);
+    ptx::mbar_init(bar(Plan::kXEmpty), KV ? 1 : 256);  // KV: MMA commit; Q: copied to TMEM
+    ptx::mbar_init(bar(Plan::kXTFull), 256);
+    ptx::mbar_init(bar(Plan::kXTFree), 1);
+    ptx::mbar_init(bar(Plan::kT1Full), 1);
+    ptx::mbar_init(bar(Plan::kT1Free), 256);
     for (int h = 0; h < 2; ++h) {
-      ptx::mbar_init(bar(Plan::kT1Full + h), 1);
       ptx::mbar_init(bar(Plan::kT2Full + h), 1);
-      ptx::mbar_init(bar(Plan::kPFull + h), 128);
-      ptx::mbar_init(bar(Plan::kDSFull + h), 128);
-      ptx::mbar_init(bar(Plan::kTFree + h), 1);
+      ptx::mbar_init(bar(Plan::kT2Free + h), 1);
+      ptx::mbar_init(bar(Plan::kPdSFull + h), 128);
+      ptx::mbar_init(bar(Plan::kStatsFull + h), 1);
+      ptx::mbar_init(bar(Plan::kStatsEmpty + h), 256);
     }
     ptx::mbar_init(bar(Plan::kAccFull), 1);
     ptx::mbar_init(bar(Plan::kAccEmpty), 256);
@@ -263,6 +320,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
 
   if (warp < C::kWarpMma) {
     // ======================================================== elementwise ===
+    ptx::setmaxnreg_inc<C::kRegsElementwise>();
     const int quarter = warp & 3;
     const int half = warp >> 2;          // column half of the 128 x 128 tile
     const int r = quarter * 32 + lane;   // row (TMEM lane)
@@ -271,8 +329,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     const uint32_t tT2 = tmem + lane_off + (uint32_t)(C::kT2 + 64 * half);
     const float* stats = reinterpret_cast<const float*>(smem + Plan::kStats);
     const float c = p.scale_log2;
-    Ring<NS> ring;
-    uint32_t t1_par = 0, t2_par = 0, af_par = 0;
+    uint32_t t1_par = 0, t2_par = 0, af_par = 0, x_par = 0, xt_par = 0;
+    int items_seen = 0;
+    int gstep = 0;  // steps processed by this CTA
     bool ok = true;
     ItemReader reader;
     while (ok) {
@@ -280,30 +339,56 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
       const BwdItem it = decode_bwd<KV, WIN>(t, p);
       const int nq = it.hi - it.lo;
-      // Q pass: this thread's query row statistics, fixed for the item.
-      float row_lse2 = 0.f, row_delta = 0.f;
+      float row_nlse2 = 0.f, row_ndelta = 0.f;
       if (!KV) {
+        // Q pass: this thread's query row statistics, fixed for the item.
         const long long idx = ((long long)it.b * p.H + it.hx) * p.Npad + it.blk * kBlockM + r;
-        row_lse2 = p.lse2[idx];
-        row_delta = p.delta[idx];
+        row_nlse2 = p.nlse2[idx];
+        row_ndelta = p.ndelta[idx];
+        // Copy the item's Q (warpgroup 0) or dO (warpgroup 1) row r from the swizzled
+        // shared-memory tile into TMEM as 16-bit pairs: the A operand of the score GEMMs.
+        if (!(ok = W.wait_warp(bar(Plan::kXFull), x_par))) break;
+        x_par ^= 1;
+        if (items_seen > 0) {  // the previous item's last score GEMMs read the TMEM copy
+          if (!(ok = W.wait_warp(bar(Plan::kXTFree), xt_par))) break;
+          xt_par ^= 1;
+          ptx::tc_fence_after();
+        }
+        const uint32_t src = sbase + (half ? Plan::kX2 : Plan::kX1) + r * 128;
+        const uint32_t dst = tmem + lane_off + (uint32_t)(half ? C::kXdO : C::kXQ);
+#pragma unroll
+        for (int cc = 0; cc < D / 64; ++cc) {
+          uint32_t x[32];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint4 q4 = ptx::ld_shared_v4(src + cc * Plan::kChunkBytes + ((u ^ (r & 7)) << 4));
+            x[4 * u] = q4.x;
+            x[4 * u + 1] = q4.y;
+            x[4 * u + 2] = q4.z;
+            x[4 * u + 3] = q4.w;
+          }
+          ptx::tmem_st32(dst + cc * 32, x);
+        }
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(Plan::kXTFull));
+        ptx::mbar_arrive(bar(Plan::kXEmpty));  // the shared-memory tiles may be refilled
       }
-      for (int s = 0; s < it.nsteps && ok; ++s) {
+      ++items_seen;
+      for (int s = 0; s < it.nsteps && ok; ++s, ++gstep) {
         const int ytile = it.lo + (KV ? s % nq : s);
-        // KV pass: the stage holding this step's Q tile also holds its lse2/delta.
-        const int st1 = ring.stage;
-        const uint32_t ph1 = ring.phase;
-        ring.next();
-        ring.next();
-        const float* st_lse = stats + st1 * 256 + 64 * half;
-        const float* st_delta = st_lse + 128;
-        if (KV && !(ok = W.wait_warp(bar(Plan::kRingFull + st1), ph1))) break;
+        // KV pass: -lse2 / -delta of this step's query tile (double-buffered by step).
+        const int sslot = gstep & 1;
+        const float* st_nlse = stats + sslot * 256 + 64 * half;
+        const float* st_ndelta = st_nlse + 128;
+        if (KV && !(ok = W.wait_warp(bar(Plan::kStatsFull + sslot), (uint32_t)(gstep >> 1) & 1u))) break;
         // Mask geometry: qi - kj = dq0 + (KV ? col - row : row - col).
         const int it_q = KV ? ytile : it.blk;
         const int jb_k = KV ? it.blk : ytile;
         const int dq0 = (it_q - jb_k) * kBlockM;
         const bool masked = (p.causal && it_q == jb_k) || (WIN && dq0 + kBlockM - 1 > p.window);
         const int colbase = 64 * half;
-        if (!(ok = W.wait_warp(bar(Plan::kT1Full + half), t1_par))) break;
+        if (!(ok = W.wait_warp(bar(Plan::kT1Full), t1_par))) break;
         t1_par ^= 1;
         ptx::tc_fence_after();
         float pv[64];
@@ -314,21 +399,24 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v[0]);
           ptx::reg_fence32(v[1]);
+          // S is in registers: the next score GEMM may overwrite T1.
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(bar(Plan::kT1Free));
           if (KV) {
 #pragma unroll
             for (int e = 0; e < 64; e += 4) {
-              const float4 l4 = *reinterpret_cast<const float4*>(st_lse + e);
+              const float4 l4 = *reinterpret_cast<const float4*>(st_nlse + e);
               const float2 x0 = __ffma2_rn(make_float2(__uint_as_float(v[e >> 5][e & 31]), __uint_as_float(v[e >> 5][(e & 31) + 1])),
-                                           make_float2(c, c), make_float2(-l4.x, -l4.y));
+                                           make_float2(c, c), make_float2(l4.x, l4.y));
               const float2 x1 = __ffma2_rn(make_float2(__uint_as_float(v[e >> 5][(e & 31) + 2]), __uint_as_float(v[e >> 5][(e & 31) + 3])),
-                                           make_float2(c, c), make_float2(-l4.z, -l4.w));
+                                           make_float2(c, c), make_float2(l4.z, l4.w));
               pv[e] = x0.x;
               pv[e + 1] = x0.y;
               pv[e + 2] = x1.x;
               pv[e + 3] = x1.y;
             }
           } else {
-            const float2 nl = make_float2(-row_lse2, -row_lse2);
+            const float2 nl = make_float2(row_nlse2, row_nlse2);
 #pragma unroll
             for (int e = 0; e < 64; e += 2) {
               const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[e >> 5][e & 31]), __uint_as_float(v[e >> 5][(e & 31) + 1])),
@@ -345,17 +433,26 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             if ((p.causal && dqk < 0) || (WIN && dqk > p.window)) pv[e] = -INFINITY;
           }
         }
+        if (masked || kEmu == 0) {
 #pragma unroll
-        for (int e = 0; e < 64; ++e) pv[e] = ptx::ex2(pv[e]);  // masked: exactly 0
+          for (int e = 0; e < 64; ++e) pv[e] = ptx::ex2(pv[e]);  // masked: exactly 0
+        } else {
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            if (((e >> 1) & 7) < kEmu) {
+              const float2 y = exp2_poly_pair(make_float2(pv[e], pv[e + 1]));
+              pv[e] = y.x;
+              pv[e + 1] = y.y;
+            } else {
+              pv[e] = ptx::ex2(pv[e]);
+              pv[e + 1] = ptx::ex2(pv[e + 1]);
+            }
+          }
+        }
+        uint32_t pk_p[32];
         if (KV) {
-          // P^T packed into this warpgroup's first 32 T1 columns: the A operand of dV.
-          uint32_t pk[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) pk[e] = DType<T>::pack(pv[2 * e], pv[2 * e + 1]);
-          ptx::tmem_st32(tT1, pk);
-          ptx::tmem_wait_st();
-          ptx::tc_fence_before();
-          ptx::mbar_arrive(bar(Plan::kPFull + half));
+          for (int e = 0; e < 32; ++e) pk_p[e] = DType<T>::pack(pv[2 * e], pv[2 * e + 1]);
         }
         if (!(ok = W.wait_warp(bar(Plan::kT2Full + half), t2_par))) break;
         t2_par ^= 1;
@@ -367,32 +464,39 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v[0]);
           ptx::reg_fence32(v[1]);
-          uint32_t pk[32];
+          // dP is in registers; P_h goes into this warpgroup's first 32 T2 columns now, so
+          // its packed registers die before dS is formed.
+          if (KV) ptx::tmem_st32(tT2, pk_p);
+          uint32_t pk_s[32];
           if (KV) {
 #pragma unroll
-            for (int e = 0; e < 64; e += 4) {
-              const float4 d4 = *reinterpret_cast<const float4*>(st_delta + e);
-              const float a0 = pv[e] * (__uint_as_float(v[e >> 5][e & 31]) - d4.x);
-              const float a1 = pv[e + 1] * (__uint_as_float(v[e >> 5][(e & 31) + 1]) - d4.y);
-              const float a2 = pv[e + 2] * (__uint_as_float(v[e >> 5][(e & 31) + 2]) - d4.z);
-              const float a3 = pv[e + 3] * (__uint_as_float(v[e >> 5][(e & 31) + 3]) - d4.w);
-              pk[e >> 1] = DType<T>::pack(a0, a1);
-              pk[(e >> 1) + 1] = DType<T>::pack(a2, a3);
+            for (int e = 0; e < 64; e += 4) {  // dS = P (dP - delta), two lanes per instruction
+              const float4 d4 = *reinterpret_cast<const float4*>(st_ndelta + e);
+              const float2 a01 = __fmul2_rn(make_float2(pv[e], pv[e + 1]),
+                                            __fadd2_rn(make_float2(__uint_as_float(v[e >> 5][e & 31]), __uint_as_float(v[e >> 5][(e & 31) + 1])),
+                                                       make_float2(d4.x, d4.y)));
+              const float2 a23 = __fmul2_rn(make_float2(pv[e + 2], pv[e + 3]),
+                                            __fadd2_rn(make_float2(__uint_as_float(v[e >> 5][(e & 31) + 2]), __uint_as_float(v[e >> 5][(e & 31) + 3])),
+                                                       make_float2(d4.z, d4.w)));
+              pk_s[e >> 1] = DType<T>::pack(a01.x, a01.y);
+              pk_s[(e >> 1) + 1] = DType<T>::pack(a23.x, a23.y);
             }
+            ptx::tmem_st32(tT2 + 32, pk_s);  // dS_h after P_h
+            ptx::mbar_arrive(bar(Plan::kStatsEmpty + sslot));  // statistics read
           } else {
+            const float2 nd = make_float2(row_ndelta, row_ndelta);
 #pragma unroll
             for (int e = 0; e < 64; e += 2) {
-              const float a0 = pv[e] * (__uint_as_float(v[e >> 5][e & 31]) - row_delta);
-              const float a1 = pv[e + 1] * (__uint_as_float(v[e >> 5][(e & 31) + 1]) - row_delta);
-              pk[e >> 1] = DType<T>::pack(a0, a1);
+              const float2 a = __fmul2_rn(make_float2(pv[e], pv[e + 1]),
+                                          __fadd2_rn(make_float2(__uint_as_float(v[e >> 5][e & 31]), __uint_as_float(v[e >> 5][(e & 31) + 1])), nd));
+              pk_s[e >> 1] = DType<T>::pack(a.x, a.y);
             }
+            ptx::tmem_st32(tT2, pk_s);
           }
-          // dS packed into this warpgroup's first 32 T2 columns: the A operand of dK / dQ.
-          ptx::tmem_st32(tT2, pk);
           ptx::tmem_wait_st();
         }
         ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(Plan::kDSFull + half));
+        ptx::mbar_arrive(bar(Plan::kPdSFull + half));
       }
       if (!ok) break;
       // ---- epilogue: Acc1 * scale -> out1 (dK | dQ), Acc2 -> out2 (dV) ----
@@ -428,28 +532,35 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       ptx::mbar_arrive(bar(Plan::kAccEmpty));
     }
   } else if (warp == C::kWarpMma) {
+    ptx::setmaxnreg_dec<C::kRegsOther>();
     // ================================================================ MMA ===
-    // Each 128 x 128 step is issued as two column halves h (64 streaming rows each), so
-    // the tensor pipe works on one half while the elementwise warpgroup of the other
-    // half runs. Issue order per step s:
-    //   G1_0 G2_0 G1_1 G2_1 | G3_0 G4_0 G3_1 G4_1
-    // with G1_h: T1_h = X1 Y1_h^T, G2_h: T2_h = X2 Y2_h^T (128 x 64 x D each), G3_h: Acc2 +=
-    // P_h Y2_h (KV pass), G4_h: Acc1 += dS_h Y1_h (128 x D x 64 each). G1_h/G2_h of step s+1
-    // wait only for G3_h/G4_h of step s (TFree_h), which were issued before G3/G4 of the
-    // other half, so the pipe never drains between steps.
-    constexpr uint32_t idNT = make_idesc<T>(kBlockM, 64, false);  // T_h = X Y_h^T
-    constexpr uint32_t idAcc = make_idesc<T>(kBlockM, D, true);   // Acc += A_h(TMEM) Y_h
+    // Issue order, software-pipelined across steps (s = step, all 128 x 128 tiles):
+    //   G1(s)      T1 = X1 Y1(s)^T          after the elementwise warps read S(s-1)
+    //   A(s-1)     accumulating GEMMs of the previous step (as its P / dS halves arrive):
+    //              KV: dV += P^T dO, dK += dS^T Q;  Q pass: dQ += dS K
+    //   G2(s)      T2 = X2 Y2(s)^T          after A(s-1) completed (it reads T2)
+    // so the score GEMM of step s runs while the elementwise warps work on step s-1.
+    constexpr uint32_t idNT = make_idesc<T>(kBlockM, kBlockN, false);  // T1 = X Y^T
+    constexpr uint32_t idNT64 = make_idesc<T>(kBlockM, 64, false);     // T2_h = X Y_h^T
+    constexpr uint32_t idAcc = make_idesc<T>(kBlockM, D, true);        // Acc += A_h(TMEM) Y_h
     constexpr uint32_t kHalfRows = 64 * 128;  // byte offset of row 64 inside a 128-row chunk
+    // dP as two 64-column GEMMs. Free in the Q pass (A = dO from TMEM, B 2 KB per
+    // instruction); in the KV pass both operands come from shared memory and a 64-wide
+    // instruction reads 6 KB in 32 tensor cycles (it runs at 48).
+    constexpr bool kSplitDP = !KV || APEX_BWD_SPLIT_DP_KV;
     const uint32_t sX1 = sbase + Plan::kX1;
     const uint32_t sX2 = sbase + Plan::kX2;
     const uint32_t sRing = sbase + Plan::kRing;
-    auto gemm_nt = [&](uint32_t d_tmem, uint32_t sA, uint32_t sB) {
+    // T = X Y^T over D (Y: 128 rows, or 64 from sB with idesc idNT64): X from shared memory
+    // (KV pass) or from TMEM (Q pass, x_tmem).
+    auto gemm_nt = [&](uint32_t d_tmem, uint32_t sA, uint32_t x_tmem, uint32_t sB, uint32_t idesc) {
       const uint64_t a0 = make_sdesc_sw128(sA, 16, 1024);
       const uint64_t b0 = make_sdesc_sw128(sB, 16, 1024);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (uint32_t)((kk >> 2) * Plan::kChunkBytes + (kk & 3) * 32) >> 4;
-        ptx::umma_ss_warp(d_tmem, a0 + off, b0 + off, idNT, kk > 0 ? 1u : 0u);
+        if (KV) ptx::umma_ss_warp(d_tmem, a0 + off, b0 + off, idesc, kk > 0 ? 1u : 0u);
+        else ptx::umma_ts_warp(d_tmem, x_tmem + (uint32_t)(8 * kk), b0 + off, idesc, kk > 0 ? 1u : 0u);
       }
     };
     // A: 128 x 64 16-bit operand packed in 32 TMEM columns at a_tmem; B: 64 rows x D.
@@ -462,11 +573,18 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                           (accumulate || kk > 0) ? 1u : 0u);
       }
     };
+    const uint32_t tT1 = tmem + C::kT1, tT2 = tmem + C::kT2;
     const uint32_t tAcc1 = tmem + C::kAcc1, tAcc2 = tmem + C::kAcc2;
     Ring<NS> ring;
-    uint32_t x_par = 0, tf_par = 0, pf_par = 0, df_par = 0, ae_par = 0;  // bit h: half h
-    int steps_done = 0, items_done = 0;
+    uint32_t x_par = 0, t1f_par = 0, t2f_par = 0, pds_par = 0, ae_par = 0;  // bit h: half h
+    int steps_issued = 0, items_accumulated = 0;
     bool ok = true;
+    struct Pending {
+      bool valid;
+      int st1, st2;
+      bool first, last;  // first / last step of its item
+    };
+    Pending pend{false, 0, 0, false, false};
     auto acquire = [&]() -> int {
       const int st = ring.stage;
       const uint32_t ph = ring.phase;
@@ -475,10 +593,36 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       ptx::tc_fence_after();
       return st;
     };
-    auto wait_bit = [&](int slot, uint32_t& par, int h) -> bool {
-      if (!W.wait_warp(bar(slot + h), (par >> h) & 1u)) return false;
-      par ^= 1u << h;
-      ptx::tc_fence_after();
+    // A(step): accumulating GEMMs of a step whose G1, G2 were issued earlier.
+    auto accumulate = [&](const Pending& pd) -> bool {
+      if (pd.first && items_accumulated > 0) {  // the epilogue must have drained the accumulators
+        if (!W.wait_warp(bar(Plan::kAccEmpty), ae_par)) return false;
+        ae_par ^= 1;
+        ptx::tc_fence_after();
+      }
+      const uint32_t sY1 = sRing + pd.st1 * Plan::kTileBytes;
+      const uint32_t sY2 = sRing + pd.st2 * Plan::kTileBytes;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        if (!W.wait_warp(bar(Plan::kPdSFull + h), (pds_par >> h) & 1u)) return false;
+        pds_par ^= 1u << h;
+        ptx::tc_fence_after();
+        const bool acc = !pd.first || h > 0;
+        const uint32_t tP = tT2 + (uint32_t)(64 * h);
+        if (KV) {
+          gemm_acc(tAcc2, tP, sY2 + h * kHalfRows, acc);       // dV += P_h^T dO_h
+          gemm_acc(tAcc1, tP + 32, sY1 + h * kHalfRows, acc);  // dK += dS_h^T Q_h
+        } else {
+          gemm_acc(tAcc1, tP, sY1 + h * kHalfRows, acc);       // dQ += dS_h K_h
+        }
+        ptx::tc_commit_warp(bar(Plan::kT2Free + h));
+      }
+      ptx::tc_commit_warp(bar(Plan::kRingEmpty + pd.st1));
+      if (KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + pd.st2));
+      if (pd.last) {
+        ptx::tc_commit_warp(bar(Plan::kAccFull));
+        ++items_accumulated;
+      }
       return true;
     };
     ItemReader reader;
@@ -486,61 +630,76 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       int t;
       if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
       const BwdItem it = decode_bwd<KV, WIN>(t, p);
-      if (!(ok = W.wait_warp(bar(Plan::kXFull), x_par))) break;
+      // Q pass: the elementwise warps copy the next item's X only after finishing this
+      // item's epilogue, which waits for the last A(); issue it before waiting for X.
+      if (!KV && pend.valid) {
+        if (!(ok = accumulate(pend))) break;
+        pend.valid = false;
+      }
+      if (!(ok = W.wait_warp(bar(KV ? Plan::kXFull : Plan::kXTFull), x_par))) break;
       x_par ^= 1;
       ptx::tc_fence_after();
       for (int s = 0; s < it.nsteps && ok; ++s) {
         const int st1 = acquire();
         ok = st1 >= 0;
         if (!ok) break;
+        if (steps_issued > 0) {  // the elementwise warps hold S(s-1) in registers
+          if (!(ok = W.wait_warp(bar(Plan::kT1Free), t1f_par))) break;
+          t1f_par ^= 1;
+          ptx::tc_fence_after();
+        }
+        gemm_nt(tT1, sX1, tmem + C::kXQ, sRing + st1 * Plan::kTileBytes, idNT);
+        ptx::tc_commit_warp(bar(Plan::kT1Full));
+        if (pend.valid) {
+          if (!(ok = accumulate(pend))) break;
+          pend.valid = false;
+        }
         const int st2 = acquire();
         ok = st2 >= 0;
         if (!ok) break;
-        const uint32_t sY1 = sRing + st1 * Plan::kTileBytes;
-        const uint32_t sY2 = sRing + st2 * Plan::kTileBytes;
+        if (kSplitDP) {
+          // dP in two column halves: half h of T2 is rewritten as soon as A_h(s-1) finished
+          // reading P_h / dS_h from it, and elementwise warpgroup h starts on it at once.
 #pragma unroll 1
-        for (int h = 0; h < 2 && ok; ++h) {
-          // T1_h, T2_h still hold P_h / dS_h of the previous step until its G3_h/G4_h finish.
-          if (steps_done > 0 && !(ok = wait_bit(Plan::kTFree, tf_par, h))) break;
-          gemm_nt(tmem + (uint32_t)(C::kT1 + 64 * h), sX1, sY1 + h * kHalfRows);
-          ptx::tc_commit_warp(bar(Plan::kT1Full + h));
-          gemm_nt(tmem + (uint32_t)(C::kT2 + 64 * h), sX2, sY2 + h * kHalfRows);
-          ptx::tc_commit_warp(bar(Plan::kT2Full + h));
-        }
-        if (!ok) break;
-        if (s == it.nsteps - 1) ptx::tc_commit_warp(bar(Plan::kXEmpty));  // last reads of X1, X2
-        if (!KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + st2));        // V: only dP reads it
-        if (s == 0 && items_done > 0) {  // the epilogue must have drained the accumulators
-          if (!(ok = W.wait_warp(bar(Plan::kAccEmpty), ae_par))) break;
-          ae_par ^= 1;
-          ptx::tc_fence_after();
-        }
-#pragma unroll 1
-        for (int h = 0; h < 2 && ok; ++h) {
-          const bool acc = s > 0 || h > 0;
-          if (KV) {
-            if (!(ok = wait_bit(Plan::kPFull, pf_par, h))) break;
-            gemm_acc(tAcc2, tmem + (uint32_t)(C::kT1 + 64 * h), sY2 + h * kHalfRows, acc);  // dV += P^T dO
+          for (int h = 0; h < 2 && ok; ++h) {
+            if (steps_issued > 0) {
+              if (!(ok = W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u))) break;
+              t2f_par ^= 1u << h;
+              ptx::tc_fence_after();
+            }
+            gemm_nt(tT2 + (uint32_t)(64 * h), sX2, tmem + C::kXdO,
+                    sRing + st2 * Plan::kTileBytes + h * kHalfRows, idNT64);
+            ptx::tc_commit_warp(bar(Plan::kT2Full + h));
           }
-          if (!(ok = wait_bit(Plan::kDSFull, df_par, h))) break;
-          gemm_acc(tAcc1, tmem + (uint32_t)(C::kT2 + 64 * h), sY1 + h * kHalfRows, acc);  // dK | dQ
-          ptx::tc_commit_warp(bar(Plan::kTFree + h));
+          if (!ok) break;
+        } else {
+          if (steps_issued > 0) {
+#pragma unroll 1
+            for (int h = 0; h < 2 && ok; ++h) {
+              ok = W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u);
+              t2f_par ^= 1u << h;
+            }
+            if (!ok) break;
+            ptx::tc_fence_after();
+          }
+          gemm_nt(tT2, sX2, tmem + C::kXdO, sRing + st2 * Plan::kTileBytes, idNT);
+          ptx::tc_commit_warp(bar(Plan::kT2Full));
+          ptx::tc_commit_warp(bar(Plan::kT2Full + 1));
         }
-        if (!ok) break;
-        if (KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + st2));
-        ptx::tc_commit_warp(bar(Plan::kRingEmpty + st1));
-        ++steps_done;
+        if (!KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + st2));  // V: only dP reads it
+        if (s == it.nsteps - 1) ptx::tc_commit_warp(bar(KV ? Plan::kXEmpty : Plan::kXTFree));  // last reads of X
+        pend = Pending{true, st1, st2, s == 0, s == it.nsteps - 1};
+        ++steps_issued;
       }
-      if (!ok) break;
-      ptx::tc_commit_warp(bar(Plan::kAccFull));
-      ++items_done;
     }
+    if (ok && pend.valid) ok = accumulate(pend);
     ptx::tc_commit_warp(bar(Plan::kDrain));
     if (lane == 0) drain_wait(bar(Plan::kDrain), 0, p.timeout_ns, p.status);
     __syncwarp();
   } else {
+    ptx::setmaxnreg_dec<C::kRegsOther>();
     // ============================================== scheduler + producer ===
-    if (lane == 0) {
+    if (warp == C::kWarpProd && lane == 0) {
       const uint64_t pol_x = ptx::policy_evict_first();  // read by this item only
       const uint64_t pol_y = ptx::policy_evict_last();   // re-read by every block of the head
       const uint32_t sX1 = sbase + Plan::kX1;
@@ -549,7 +708,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       const uint32_t sStats = sbase + Plan::kStats;
       Ring<NS> ring;
       uint32_t xe_par = 1;
-      int fills = 0, x_fills = 0;
+      int fills = 0, x_fills = 0, stat_fills = 0;
       bool ok = true;
       auto load_tile = [&](uint32_t dst, const CUtensorMap* map, uint32_t b, int row0, int h, int bi,
                            uint64_t pol) {
@@ -585,17 +744,21 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             const uint32_t ph = ring.phase;
             ring.next();
             if (!(ok = W.wait(bar(Plan::kRingEmpty + st), ph ^ 1))) break;
-            const bool with_stats = KV && k == 0;
-            ptx::mbar_arrive_expect_tx(bar(Plan::kRingFull + st),
-                                       (uint32_t)Plan::kTileBytes + (with_stats ? 1024u : 0u));
+            ptx::mbar_arrive_expect_tx(bar(Plan::kRingFull + st), (uint32_t)Plan::kTileBytes);
             load_tile(sRing + st * Plan::kTileBytes, k == 0 ? &tmY1 : &tmY2, bar(Plan::kRingFull + st),
                       ytile * kBlockN, hy, it.b, pol_y);
-            if (with_stats) {
-              const long long idx = ((long long)it.b * p.H + hy) * p.Npad + (long long)ytile * kBlockM;
-              ptx::bulk_load(sStats + st * Plan::kStatsBytes, p.lse2 + idx, 512u, bar(Plan::kRingFull + st), pol_y);
-              ptx::bulk_load(sStats + st * Plan::kStatsBytes + 512, p.delta + idx, 512u, bar(Plan::kRingFull + st), pol_y);
-            }
             ++fills;
+          }
+          if (KV && ok) {
+            // lse2 / delta of the query tile into stats slot (step & 1), after the
+            // elementwise warps released it (two steps back).
+            const int sslot = stat_fills & 1;
+            if (!(ok = W.wait(bar(Plan::kStatsEmpty + sslot), ((uint32_t)(stat_fills >> 1) & 1u) ^ 1u))) break;
+            const long long idx = ((long long)it.b * p.H + hy) * p.Npad + (long long)ytile * kBlockM;
+            ptx::mbar_arrive_expect_tx(bar(Plan::kStatsFull + sslot), 1024u);
+            ptx::bulk_load(sStats + sslot * Plan::kStatsBytes, p.nlse2 + idx, 512u, bar(Plan::kStatsFull + sslot), pol_y);
+            ptx::bulk_load(sStats + sslot * Plan::kStatsBytes + 512, p.ndelta + idx, 512u, bar(Plan::kStatsFull + sslot), pol_y);
+            ++stat_fills;
           }
         }
       }
@@ -606,6 +769,8 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         drain_wait(bar(Plan::kRingFull + (f % NS)), (uint32_t)((f / NS) & 1), p.timeout_ns, p.status);
       }
       if (x_fills > 0) drain_wait(bar(Plan::kXFull), (uint32_t)((x_fills - 1) & 1), p.timeout_ns, p.status);
+      for (int k = stat_fills > 2 ? stat_fills - 2 : 0; k < stat_fills; ++k)
+        drain_wait(bar(Plan::kStatsFull + (k & 1)), (uint32_t)(k >> 1) & 1u, p.timeout_ns, p.status);
     }
     __syncwarp();
   }

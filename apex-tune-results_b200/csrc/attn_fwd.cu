@@ -382,7 +382,7 @@ constexpr int kBwdBlock = apex::kBlockM;
 
 long long bwd_padded_rows(int seqlen) { return ((long long)seqlen + kBwdBlock - 1) / kBwdBlock * kBwdBlock; }
 
-// Workspace: lse2 then delta, each fp32 [batch * heads_q][Npad].
+// Workspace: -lse2 then -delta, each fp32 [batch * heads_q][Npad].
 size_t bwd_workspace_bytes(int batch, int heads_q, int seqlen) {
   if (batch <= 0 || heads_q <= 0 || seqlen <= 0) return 0;
   return (size_t)2 * (size_t)batch * (size_t)heads_q * (size_t)bwd_padded_rows(seqlen) * sizeof(float);
@@ -422,8 +422,8 @@ int launch_bwd(DeviceState& ds, const apex_attn_bwd_args& a, const CUtensorMap& 
   if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
 
   apex::BwdParams p{};
-  p.lse2 = lse2;
-  p.delta = delta;
+  p.nlse2 = lse2;
+  p.ndelta = delta;
   p.status = ds.status;
   p.B = a.batch;
   p.H = a.heads_q;
