@@ -3,7 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {apex,reference}]
 
 N = 1: the BASELINE.json headline workload C3 (B=4, H=32, N=8192, d=128, bf16, causal,
-with the fp32 logsumexp), plus C2 (d=64) and C4 (d=256, once built) as extra entries.
+with the fp32 logsumexp), plus C2 (d=64) and C4 (d=256) as extra entries, and the
+backward (dq, dk, dv) at the C3 and C2 shapes next to torch's SDPA backward on the same GPU.
 A "step" is one forward over the whole batch. value = causal FLOP (2*B*H*N^2*d,
 submission.py:235-240) per second over the K timed steps, device-timed with CUDA events,
 inputs resident in HBM (q/k/v = 805 MB, larger than the 126 MB L2, so no flush).
@@ -42,6 +43,10 @@ CONFIGS = {
     "C4": dict(B=2, H=16, N=8192, D=256),
     "C5": dict(B=8, H=64, N=16384, D=128),
 }
+# Backward profiling cases (--only-bwd): the C2 / C3 shapes and a one-batch C3 slice whose
+# inputs (5 x 67 MB) still exceed L2 but keep an ncu capture short.
+BWD_PROFILE_CONFIGS = {"C2": CONFIGS["C2"], "C3": CONFIGS["C3"],
+                       "C3b1": dict(B=1, H=32, N=8192, D=128)}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # The MLS-Bench shapes the reference publishes numbers for (fp16, causal;
 # mls-bench_fused_attention/bench.py:23-27) and its published H100 TFLOP/s for them
@@ -196,6 +201,53 @@ def bench_mls_shapes(steps, warmup, device):
                         "vs_published_h100": round(t / PUBLISHED_H100_TFLOPS[d], 3)}
         del q, k, v
     return out
+
+
+def bench_backward(name, c, steps, warmup, device):
+    """Causal attention backward (dq, dk, dv for an upstream gradient) at config `c`: this
+    library's sm_100a backward and torch's SDPA backward (cuDNN / flash) on the same GPU.
+    FLOP convention: 2.5 x the forward's (five N^2 d GEMMs against the forward's two, as
+    flash-attention reports backward throughput). Parity: dq, dk, dv of (b, h) = (0, 0)
+    against fp32 autograd of the explicit attention, |err| <= 2.5e-2 + 2^-7 |ref|."""
+    import torch.nn.functional as F
+    from apex_attn import custom_attention_backward, custom_attention_forward
+    stream = torch.cuda.current_stream(device)
+    q, k, v = make_device_inputs(c, 7, device)
+    g = torch.Generator(device=device).manual_seed(8)
+    do = torch.randn(q.shape, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+    o, lse = custom_attention_forward(q, k, v, causal=True, return_lse=True)
+    ms, _ = time_device(lambda: custom_attention_backward(q, k, v, o, lse, do, causal=True),
+                        steps, warmup, stream)
+    dq, dk, dv = custom_attention_backward(q, k, v, o, lse, do, causal=True)
+    # parity on one head
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    qh, kh, vh = (t[0, 0].float().requires_grad_(True) for t in (q, k, v))
+    n = c["N"]
+    s = (qh @ kh.T / math.sqrt(c["D"])).masked_fill(
+        torch.ones(n, n, dtype=torch.bool, device=device).triu(1), float("-inf"))
+    (torch.softmax(s, dim=-1) @ vh).backward(do[0, 0].float())
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    ratio = 0.0
+    for got, ref in ((dq, qh.grad), (dk, kh.grad), (dv, vh.grad)):
+        bound = 2.5e-2 + 2.0 ** -7 * ref.abs()
+        ratio = max(ratio, ((got[0, 0].float() - ref).abs() / bound).max().item())
+    del s, qh, kh, vh
+    # torch SDPA backward on the same inputs
+    qs, ks, vs = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+    os_ = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True)
+    sdpa_ms, _ = time_device(lambda: torch.autograd.grad(os_, (qs, ks, vs), do, retain_graph=True),
+                             steps, warmup, stream)
+    f = 2.5 * flops(c)
+    peaks, _ = load_peaks()
+    t = f * steps / (ms * 1e-3) / 1e12
+    ts = f * steps / (sdpa_ms * 1e-3) / 1e12
+    return {"config": c, "tflops": round(t, 1), "ms_per_step": round(ms / steps, 4),
+            "frac_of_peak": round(t / peaks["bf16_tflops"], 4),
+            "sdpa_tflops_same_gpu": round(ts, 1), "speedup_vs_sdpa": round(t / ts, 3),
+            "flop_per_step": f, "flop_convention": "2.5 x forward (5 GEMMs of 2 N^2 d / 2, causal)",
+            "parity_worst_err_over_bound": round(ratio, 3),
+            "launches_per_step": "prep + dK/dV pass + dQ pass (+ 2 counter memsets)"}
 
 
 def bench_e2e(c, steps, warmup, device):
@@ -382,6 +434,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--only", choices=sorted(CONFIGS), default=None,
                     help="run only the device-resident kernel leg of one config (profiling)")
+    ap.add_argument("--only-bwd", choices=sorted(BWD_PROFILE_CONFIGS), default=None,
+                    help="run only the backward of one config, device-resident (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -426,6 +480,18 @@ def main():
     torch.cuda.set_device(device)
     import apex_attn
     peaks, peak_kind = load_peaks()
+    if args.only_bwd:
+        from apex_attn import custom_attention_backward, custom_attention_forward
+        c = BWD_PROFILE_CONFIGS[args.only_bwd]
+        q, k, v = make_device_inputs(c, 7, device)
+        do = torch.randn(q.shape, device=device, dtype=torch.float32).to(torch.bfloat16)
+        o, lse = custom_attention_forward(q, k, v, causal=True, return_lse=True)
+        ms, _ = time_device(lambda: custom_attention_backward(q, k, v, o, lse, do, causal=True),
+                            args.steps, args.warmup, torch.cuda.current_stream(device))
+        t = 2.5 * flops(c) * args.steps / (ms * 1e-3) / 1e12
+        print(json.dumps({"backward": args.only_bwd, **c, "tflops": t, "ms_per_step": ms / args.steps,
+                          "device_status": apex_attn.device_status()}))
+        return
     if args.only:
         c = CONFIGS[args.only]
         r = bench_config(args.only, c, args.steps, args.warmup, device)
@@ -445,6 +511,8 @@ def main():
                        "frac_of_peak": round(r["tflops"] / peaks["bf16_tflops"], 4),
                        "kernel_tflops": round(ach, 1), "config": c}
     mls = bench_mls_shapes(max(3, min(args.steps, 10)), 3, device)
+    bwd = {name: bench_backward(name, CONFIGS[name], max(3, min(args.steps, 10)), 3, device)
+           for name in ("C3", "C2")}
     e2e = bench_e2e(c3, max(3, min(args.steps, 10)), 3, device)
     status = apex_attn.device_status()
     cpu_v, cores, sample = cpu_reference(c3, budget_s=args.cpu_budget)
@@ -471,6 +539,7 @@ def main():
         "clocks": clocks,
         "per_config": extra,
         "mls_bench_fp16": mls,
+        "backward": bwd,
         "device_status": status,
     }
     print(json.dumps(line))
