@@ -54,6 +54,16 @@ class BwdArgs(ctypes.Structure):
                 ("sm_scale", ctypes.c_float), ("strides", ctypes.c_longlong * 24)]
 
 
+class VarlenArgs(ctypes.Structure):
+    """Mirror of apex_attn_varlen_args (include/apex_attn.h)."""
+    _fields_ = [("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+                ("o", ctypes.c_void_p), ("lse", ctypes.c_void_p), ("cu_seqlens", ctypes.c_void_p),
+                ("batch", ctypes.c_int), ("heads_q", ctypes.c_int), ("heads_kv", ctypes.c_int),
+                ("total", ctypes.c_int), ("max_seqlen", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("dtype", ctypes.c_int), ("causal", ctypes.c_int), ("window_left", ctypes.c_int),
+                ("sm_scale", ctypes.c_float), ("strides", ctypes.c_longlong * 8)]
+
+
 # Every symbol the header declares: (name, restype, argtypes).
 _c_ll_p = ctypes.POINTER(ctypes.c_longlong)
 SYMBOLS = {
@@ -64,6 +74,7 @@ SYMBOLS = {
          ctypes.c_float, _c_ll_p, ctypes.c_void_p],
     ),
     "apex_attn_fwd_ex": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.c_void_p]),
+    "apex_attn_fwd_varlen": (ctypes.c_int, [ctypes.POINTER(VarlenArgs), ctypes.c_void_p]),
     "apex_attn_fwd_noalloc": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

@@ -98,6 +98,63 @@ def custom_attention_forward(q, k, v, causal=True, sm_scale=None, return_lse=Fal
     return (o, lse) if return_lse else o
 
 
+def custom_attention_varlen_forward(q, k, v, cu_seqlens, max_seqlen, causal=True, sm_scale=None,
+                                    return_lse=False, window_left=None):
+    """Attention over a packed batch of variable-length sequences (flash-attn's varlen
+    layout): q [total, H, D], k and v [total, H_kv, D]; sequence b is rows
+    cu_seqlens[b] .. cu_seqlens[b+1] - 1 (int32 CUDA tensor of batch + 1 offsets, cu[0] = 0,
+    nondecreasing, cu[-1] = total); max_seqlen is the longest sequence. Each sequence
+    attends only within itself (causal / window relative to its first row). Returns o
+    [total, H, D] (rows outside every sequence are left as zeros) and, with return_lse,
+    the fp32 logsumexp [H, total]. Head dims 64, 128, 256; bf16 or fp16; GQA as for the
+    batched operator.
+    """
+    if q.dim() != 3 or k.dim() != 3 or k.shape != v.shape:
+        raise ValueError(f"q, k, v must be [total, H, D] with k and v alike, got {tuple(q.shape)}, "
+                         f"{tuple(k.shape)}, {tuple(v.shape)}")
+    total, nheads, headdim = q.shape
+    kv_heads = k.shape[1]
+    if (k.shape[0], k.shape[2]) != (total, headdim) or nheads % kv_heads != 0:
+        raise ValueError("k and v must be [total, H_kv, D] with H_kv dividing q's heads")
+    if not supports_head_dim(headdim):
+        raise KeyError(headdim)
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError(f"q, k, v must all be float16 or bfloat16, got {q.dtype}, {k.dtype}, {v.dtype}")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.dim() != 1 or cu_seqlens.numel() < 2:
+        raise ValueError("cu_seqlens must be a 1-D int32 tensor of batch + 1 offsets")
+    if not all(t.is_cuda and t.device == q.device for t in (q, k, v, cu_seqlens)):
+        raise ValueError("q, k, v, cu_seqlens must be CUDA tensors on one device")
+    if window_left is not None and (window_left < 0 or not causal):
+        raise ValueError("window_left must be >= 0 and needs causal=True")
+    if int(max_seqlen) <= 0:
+        raise ValueError("max_seqlen must be positive")
+
+    def ready(t):
+        if t.stride(-1) != 1 or t.data_ptr() % 16 != 0 or any(s % 8 for s in t.stride()[:2]):
+            return t.contiguous()
+        return t
+    q, k, v = ready(q), ready(k), ready(v)
+    cu_seqlens = cu_seqlens.contiguous()
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(headdim)
+    o = torch.zeros(q.shape, dtype=q.dtype, device=q.device)
+    lse = torch.zeros((nheads, total), dtype=torch.float32, device=q.device) if return_lse else None
+    if total == 0:
+        return (o, lse) if return_lse else o
+    strides = [q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+               o.stride(0), o.stride(1)]
+    args = _lib.VarlenArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), o=o.data_ptr(),
+                           lse=lse.data_ptr() if lse is not None else None,
+                           cu_seqlens=cu_seqlens.data_ptr(), batch=cu_seqlens.numel() - 1,
+                           heads_q=nheads, heads_kv=kv_heads, total=total, max_seqlen=int(max_seqlen),
+                           head_dim=headdim, dtype=_DTYPES[q.dtype], causal=1 if causal else 0,
+                           window_left=-1 if window_left is None else int(window_left),
+                           sm_scale=float(sm_scale), strides=(ctypes.c_longlong * 8)(*strides))
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    _lib.check(_lib.load().apex_attn_fwd_varlen(ctypes.byref(args), stream), "custom_attention_varlen_forward")
+    return (o, lse) if return_lse else o
+
+
 def custom_attention_backward(q, k, v, o, lse, dout, causal=True, sm_scale=None, window_left=None):
     """Gradients (dq, dk, dv) of custom_attention_forward for the upstream gradient `dout`.
 

@@ -211,10 +211,10 @@ int encode_map(CUtensorMap* m, const void* ptr, int dtype, int B, int H, int N, 
   return r == CUDA_SUCCESS ? APEX_ATTN_OK : APEX_ATTN_ERR_TENSOR_MAP;
 }
 
-template <int D, typename T, bool WIN>
+template <int D, typename T, bool WIN, bool VAR>
 int launch_one(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
                const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
-  auto kern = apex::attn_fwd_sm100_kernel<D, T, kEmu<D>, WIN>;
+  auto kern = apex::attn_fwd_sm100_kernel<D, T, kEmu<D>, WIN, VAR>;
   constexpr int smem = apex::SmemPlan<D>::kDynamicBytes;
   if (!(ds.attr_done & attr_bit)) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -229,12 +229,17 @@ int launch_one(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const 
   return APEX_ATTN_OK;
 }
 
-// attr_bit covers the (D, T) pair; the windowed instantiation uses the next bit up.
+// attr_bit covers the (D, T) pair; the windowed instantiations shift it by 8, the packed
+// variable-length ones by 16.
 template <int D, typename T>
 int launch(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
            const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
-  if (p.window >= 0) return launch_one<D, T, true>(ds, attr_bit << 8, mq, mk, mv, p, grid, stream);
-  return launch_one<D, T, false>(ds, attr_bit, mq, mk, mv, p, grid, stream);
+  const bool win = p.window >= 0;
+  if (p.cu_seqlens != nullptr)
+    return win ? launch_one<D, T, true, true>(ds, attr_bit << 24, mq, mk, mv, p, grid, stream)
+               : launch_one<D, T, false, true>(ds, attr_bit << 16, mq, mk, mv, p, grid, stream);
+  return win ? launch_one<D, T, true, false>(ds, attr_bit << 8, mq, mk, mv, p, grid, stream)
+             : launch_one<D, T, false, false>(ds, attr_bit, mq, mk, mv, p, grid, stream);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -280,6 +285,10 @@ __global__ void wait_timeout_selftest_kernel(int* status, unsigned long long tim
 
 bool supported_head_dim(int head_dim) { return head_dim == 64 || head_dim == 128 || head_dim == 256; }
 
+int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUtensorMap& mq,
+                        const CUtensorMap& mk, const CUtensorMap& mv, int head_dim, int dtype,
+                        void* stream);
+
 // Validation, tensor maps, parameters and dispatch shared by both forward entry points.
 // `noalloc` selects the allocation-free device state and clears its status word first.
 int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, float* lse, int batch,
@@ -322,30 +331,42 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   AttnParams p{};
   p.o = o;
   p.lse = lse;
-  p.status = ds->status;
   p.o_sb = strides[9];
   p.o_sh = strides[10];
   p.o_sn = strides[11];
   p.B = batch;
   p.H = heads;
   p.N = seqlen;
+  p.kv_group = heads / heads_kv;
+  p.window = window;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  return schedule_and_launch(*ds, noalloc, p, mq, mk, mv, head_dim, dtype, stream);
+}
+
+// Scheduling parameters, scratch, and the launch shared by every forward entry point. The
+// caller filled the output, shape, mask and scale fields of p.
+int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUtensorMap& mq,
+                        const CUtensorMap& mk, const CUtensorMap& mv, int head_dim, int dtype,
+                        void* stream) {
+  DeviceState* ds = &dst;
+  const long long BH = (long long)p.B * p.H;
+  const int rows_per_item = item_rows(head_dim);
+  const long long mblocks = (p.N + rows_per_item - 1) / rows_per_item;
+  p.status = ds->status;
   p.num_mblocks = (int)mblocks;
-  p.num_kblocks = (seqlen + apex::kBlockN - 1) / apex::kBlockN;
+  p.num_kblocks = (p.N + apex::kBlockN - 1) / apex::kBlockN;
   p.num_items = (int)(BH * mblocks);
   // L2 scheduling groups: keep the K/V of the heads that concurrently running CTAs stream
   // within ~48 MB of L2 (query heads that share a K/V head count once); split the heads
   // into groups whose sizes differ by at most one.
-  const double kv_bytes_per_head = 2.0 * seqlen * head_dim * 2.0 / (heads / heads_kv);
+  const double kv_bytes_per_head = 2.0 * p.N * head_dim * 2.0 / p.kv_group;
   long long g = (long long)(48.0 * 1024 * 1024 / kv_bytes_per_head);
   g = std::max(1LL, std::min(g, BH));
   const long long ngroups = (BH + g - 1) / g;
   p.group_q = (int)(BH / ngroups);
   p.group_big = (int)(BH % ngroups);
   p.work_counter = ds->status + kCounterBase + (int)(g_counter_seq.fetch_add(1) % kCounterSlots);
-  p.scale_log2 = sm_scale * 1.4426950408889634f;
-  p.causal = causal ? 1 : 0;
-  p.kv_group = heads / heads_kv;
-  p.window = window;
   p.timeout_ns = wait_timeout_ns();
   const int grid = std::min(p.num_items, ds->num_sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -375,6 +396,65 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
       return bf16 ? launch<256, __nv_bfloat16>(*ds, 16u, mq, mk, mv, p, grid, s)
                   : launch<256, __half>(*ds, 32u, mq, mk, mv, p, grid, s);
   }
+}
+
+// Packed variable-length forward (apex_attn_fwd_varlen).
+int forward_varlen(const apex_attn_varlen_args* a, void* stream) {
+  // ---- argument validation (no CUDA calls) ----
+  if (!a || !a->q || !a->k || !a->v || !a->o || !a->cu_seqlens) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->batch <= 0 || a->heads_q <= 0 || a->total <= 0 || a->max_seqlen <= 0)
+    return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->heads_kv <= 0 || a->heads_q % a->heads_kv != 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->window_left < -1 || (a->window_left >= 0 && !a->causal)) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (!supported_head_dim(a->head_dim)) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
+  if (a->dtype != APEX_ATTN_BF16 && a->dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
+  if (!std::isfinite(a->sm_scale) || !(a->sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
+  const long long mblocks = (a->max_seqlen + item_rows(a->head_dim) - 1) / item_rows(a->head_dim);
+  if ((long long)a->batch * a->heads_q * mblocks > 0x7fffffffLL || a->total > (1 << 30) ||
+      a->max_seqlen > (1 << 30) || a->batch > (1 << 30))
+    return APEX_ATTN_ERR_TOO_LARGE;
+  for (int i = 0; i < 8; ++i)
+    if (a->strides[i] < 0 || (a->strides[i] & 7) != 0 || a->strides[i] >= (1LL << 38)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  for (int t = 0; t < 4; ++t)  // (token, head) per tensor: rows of one token must not overlap
+    if (a->strides[2 * t + 1] < a->head_dim) return APEX_ATTN_ERR_BAD_LAYOUT;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  if ((a->lse && (reinterpret_cast<uintptr_t>(a->lse) & 3u)) || (reinterpret_cast<uintptr_t>(a->cu_seqlens) & 3u))
+    return APEX_ATTN_ERR_BAD_LAYOUT;
+
+  // ---- device ----
+  const int dev = device_of(a->q);
+  if (dev < 0 || device_of(a->k) != dev || device_of(a->v) != dev || device_of(a->o) != dev ||
+      device_of(a->cu_seqlens) != dev)
+    return APEX_ATTN_ERR_NO_DEVICE;
+  if (a->lse && device_of(a->lse) != dev) return APEX_ATTN_ERR_NO_DEVICE;
+  DeviceGuard guard(dev);
+  DeviceState* ds = nullptr;
+  int rc = init_device(dev, &ds);
+  if (rc != APEX_ATTN_OK) return rc;
+
+  // One 4-D map per tensor over the packed rows: dims (D, total, H, 1).
+  const long long* st = a->strides;
+  CUtensorMap mq, mk, mv;
+  if ((rc = encode_map(&mq, a->q, a->dtype, 1, a->heads_q, a->total, a->head_dim, 0, st[1], st[0])) ||
+      (rc = encode_map(&mk, a->k, a->dtype, 1, a->heads_kv, a->total, a->head_dim, 0, st[3], st[2])) ||
+      (rc = encode_map(&mv, a->v, a->dtype, 1, a->heads_kv, a->total, a->head_dim, 0, st[5], st[4])))
+    return rc;
+  AttnParams p{};
+  p.o = a->o;
+  p.lse = a->lse;
+  p.o_sb = 0;
+  p.o_sh = st[7];
+  p.o_sn = st[6];
+  p.B = a->batch;
+  p.H = a->heads_q;
+  p.N = a->max_seqlen;
+  p.kv_group = a->heads_q / a->heads_kv;
+  p.window = a->window_left;
+  p.causal = a->causal ? 1 : 0;
+  p.scale_log2 = a->sm_scale * 1.4426950408889634f;
+  p.cu_seqlens = a->cu_seqlens;
+  p.total = a->total;
+  return schedule_and_launch(*ds, false, p, mq, mk, mv, a->head_dim, a->dtype, stream);
 }
 
 // ------------------------------------------------------------------ backward --
@@ -583,6 +663,10 @@ int apex_attn_fwd_ex(const apex_attn_fwd_args* a, void* stream) {
   if (!a) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   return forward(false, a->q, a->k, a->v, a->o, a->lse, a->batch, a->heads_q, a->heads_kv, a->seqlen,
                  a->head_dim, a->dtype, a->causal, a->window_left, a->sm_scale, a->strides, stream);
+}
+
+int apex_attn_fwd_varlen(const apex_attn_varlen_args* args, void* stream) {
+  return forward_varlen(args, stream);
 }
 
 int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,

@@ -67,6 +67,12 @@ struct AttnParams {
   int causal;
   int kv_group;      // query heads per K/V head (grouped-query attention; 1 = plain)
   int window;        // causal sliding window: key j visible to row i iff i - window <= j (-1: none)
+  // Packed variable-length batch (VAR kernels only): sequence b occupies rows
+  // [cu_seqlens[b], cu_seqlens[b + 1]) of tensors with `total` rows; N is the longest
+  // sequence. Offsets are clamped to [0, total] and lengths to N in the kernel, so a
+  // malformed array cannot move a load or store out of bounds.
+  const int* cu_seqlens;
+  int total;
   unsigned long long timeout_ns;
 };
 
@@ -185,6 +191,9 @@ struct SmemPlan {
 
 struct WorkItem {
   int b, h, m0;
+  int s0, len;  // first row of the item's sequence in the tensors, and its length
+  int tb;       // batch coordinate of the TMA maps (b; 0 for a packed batch)
+  int nkb;      // K/V tiles of the sequence, ceil(len / 128)
   // Query sub-tile i reads K/V tiles [lo[i], nb[i]); nb[i] = 0: sub-tile past the end.
   int lo[2], nb[2];
   int jlo, nbmax;  // K/V tiles of the item: [jlo, nbmax), the union over its sub-tiles
@@ -198,7 +207,7 @@ struct WorkItem {
 // group items run longest first (query block descending), heads interleaved. CTAs take
 // items in this order from a shared counter, so long items start early and the small
 // ones fill in at the end.
-template <int SUB, bool WIN>
+template <int SUB, bool WIN, bool VAR>
 __device__ __forceinline__ WorkItem decode_item(int t, const AttnParams& p) {
   const int MB = p.num_mblocks;
   const int q = p.group_q;
@@ -222,9 +231,22 @@ __device__ __forceinline__ WorkItem decode_item(int t, const AttnParams& p) {
   it.b = bh / p.H;
   it.h = bh - it.b * p.H;
   it.m0 = mb * SUB * kBlockM;
+  if (VAR) {
+    const int a = min(max(__ldg(p.cu_seqlens + it.b), 0), p.total);
+    const int e = min(max(__ldg(p.cu_seqlens + it.b + 1), a), p.total);
+    it.s0 = a;
+    it.len = min(e - a, p.N);
+    it.tb = 0;
+    it.nkb = (it.len + kBlockN - 1) / kBlockN;
+  } else {
+    it.s0 = 0;
+    it.len = p.N;
+    it.tb = it.b;
+    it.nkb = p.num_kblocks;
+  }
   auto tiles = [&](int r0) {
-    if (r0 >= p.N) return 0;
-    return p.causal ? min(p.num_kblocks, r0 / kBlockN + 1) : p.num_kblocks;
+    if (r0 >= it.len) return 0;
+    return p.causal ? min(it.nkb, r0 / kBlockN + 1) : it.nkb;
   };
   // First K/V tile a sub-tile starting at row r0 can see: with a sliding window, row r0
   // sees keys >= r0 - window (later rows see fewer low keys, masked per element).
@@ -356,8 +378,8 @@ struct ItemReader {
 // EMU8: of every 8 column pairs of an unmasked S tile, how many take exp2 from the
 // FMA-pipe polynomial instead of MUFU (0 = all MUFU).
 // WIN: the launch uses a causal sliding window (p.window >= 0); without it the window
-// logic compiles away.
-template <int D, typename T, int EMU8, bool WIN>
+// logic compiles away. VAR: packed variable-length batch (p.cu_seqlens).
+template <int D, typename T, int EMU8, bool WIN, bool VAR>
 __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
@@ -449,7 +471,6 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     const uint32_t sP = sbase + Plan::kP + i * Plan::kPTileBytes + r * 128;
     const float c = p.scale_log2;
     const float2 c2 = make_float2(c, c);
-    const int kv_last_valid = p.N - (p.num_kblocks - 1) * kBlockN;  // keys in last K tile
     uint32_t s_par = 0, le_par = 1, pf_par = 0;
     int p_written = 0;  // P tiles handed over so far (the buffer is reused every tile)
     bool ok = true;
@@ -457,7 +478,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     while (ok) {
       int t;
       if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-      const WorkItem it = decode_item<SUB, WIN>(t, p);
+      const WorkItem it = decode_item<SUB, WIN, VAR>(t, p);
       const int nb = it.nbi(i);
       const int lo = it.loi(i);
       if (nb == 0) continue;
@@ -485,7 +506,8 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(Plan::kSFree + i));
         const bool diag_tile = p.causal && j == diag;
-        const bool tail_tile = !p.causal && j == p.num_kblocks - 1 && kv_last_valid < kBlockN;
+        const int kv_last_valid = it.len - (it.nkb - 1) * kBlockN;  // keys in the last K tile
+        const bool tail_tile = !p.causal && j == it.nkb - 1 && kv_last_valid < kBlockN;
         // Sliding window: the tile holds keys below some row's window start iff its first
         // key is below the sub-tile's last row minus the window.
         const bool win_tile = WIN && j * kBlockN < r0 + kBlockM - 1 - p.window;
@@ -607,9 +629,9 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       ptx::tc_fence_after();
       const float inv = 1.f / l;
       const int row = it.m0 + i * kBlockM + r;
-      const bool valid = row < p.N;
-      T* orow = reinterpret_cast<T*>(p.o) + (long long)it.b * p.o_sb + (long long)it.h * p.o_sh +
-                (long long)row * p.o_sn;
+      const bool valid = row < it.len;
+      T* orow = reinterpret_cast<T*>(p.o) + (long long)it.b * p.o_sb * (VAR ? 0 : 1) +
+                (long long)it.h * p.o_sh + (long long)(it.s0 + row) * p.o_sn;
       const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
 #pragma unroll 1
       for (int ch = 0; ch < D / 32; ++ch) {
@@ -630,8 +652,12 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar(Plan::kOEmpty + i));
-      if (p.lse != nullptr && valid)
-        p.lse[((long long)it.b * p.H + it.h) * p.N + row] = (m + __log2f(l)) * 0.69314718055994531f;
+      if (p.lse != nullptr && valid) {
+        // [B, H, N]; packed batch: [H, total]
+        const long long li = VAR ? (long long)it.h * p.total + it.s0 + row
+                                 : ((long long)it.b * p.H + it.h) * p.N + row;
+        p.lse[li] = (m + __log2f(l)) * 0.69314718055994531f;
+      }
       return true;
     };
     bool ok = true;
@@ -639,7 +665,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     while (ok) {
       int t;
       if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-      const WorkItem it = decode_item<SUB, WIN>(t, p);
+      const WorkItem it = decode_item<SUB, WIN, VAR>(t, p);
       for (int i = 0; i < SUB && ok; ++i)
         if (it.nbi(i) > 0) ok = finish(it, i);
     }
@@ -749,14 +775,14 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       while (ok) {
         int t;
         if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-        const WorkItem it = decode_item<SUB, WIN>(t, p);
+        const WorkItem it = decode_item<SUB, WIN, VAR>(t, p);
         const int nb = it.nbi(i), lo = it.loi(i);  // this sub-tile reads tiles [lo, nb)
         if (nb > 0) {
           if (!(ok = W.wait_warp(bar(Plan::kQFull + i), q_par))) break;
           q_par ^= 1;
         }
         auto mine = [&](int j) { return j >= lo && j < nb; };
-        ok = do_S(mine(it.jlo));  // K(jlo)
+        if (it.nbmax > 0) ok = do_S(mine(it.jlo));  // K(jlo); an empty item (packed batch) has no tiles
         if (ok && nb > 0 && nb - 1 == it.jlo) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last use of Q_i
         for (int j = it.jlo; j < it.nbmax && ok; ++j) {
           if (j + 1 < it.nbmax) {
@@ -788,7 +814,8 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         int fills = 0;  // K/V stage fills issued
         bool q_filled = false;
         bool ok = true;
-        auto fill = [&](const CUtensorMap* map, int j, int h_idx, int b_idx) -> bool {
+        // K or V tile j of the item's sequence (rows s0 + 128 j ...).
+        auto fill = [&](const CUtensorMap* map, int j, int h_idx, int b_idx, int s0) -> bool {
           for (int h = 0; h < KP; ++h) {
             const int st = ring.stage;
             const uint32_t ph = ring.phase;
@@ -798,7 +825,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
 #pragma unroll
             for (int cc = 0; cc < C::kStageCols / 64; ++cc)
               ptx::tma_load_4d(sKV + st * Plan::kStageBytes + cc * Plan::kChunkBytes, map,
-                               bar(Plan::kKvFull + st), h * C::kStageCols + cc * 64, j * kBlockN,
+                               bar(Plan::kKvFull + st), h * C::kStageCols + cc * 64, s0 + j * kBlockN,
                                h_idx, b_idx, pol_kv);
             ++fills;
           }
@@ -825,22 +852,22 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
             break;
           }
           if (t < 0) break;
-          const WorkItem it = decode_item<SUB, WIN>(t, p);
+          const WorkItem it = decode_item<SUB, WIN, VAR>(t, p);
           if (it.nbi(qi) > 0) {
             if (!(ok = W.wait(bar(Plan::kQEmpty + qi), qe_par))) break;
             qe_par ^= 1;
             ptx::mbar_arrive_expect_tx(bar(Plan::kQFull + qi), (uint32_t)Plan::kQTileBytes);
             for (int cc = 0; cc < D / 64; ++cc)
               ptx::tma_load_4d(sQ + cc * Plan::kChunkBytes, &tmQ, bar(Plan::kQFull + qi), cc * 64,
-                               it.m0 + qi * kBlockM, it.h, it.b, pol_q);
+                               it.s0 + it.m0 + qi * kBlockM, it.h, it.tb, pol_q);
             q_filled = true;
           }
           if (qi != 0) continue;
           const int hkv = it.h / p.kv_group;  // grouped-query attention: shared K/V head
-          ok = fill(&tmK, it.jlo, hkv, it.b);
+          if (it.nbmax > 0) ok = fill(&tmK, it.jlo, hkv, it.tb, it.s0);
           for (int j = it.jlo; j < it.nbmax && ok; ++j) {
-            if (j + 1 < it.nbmax) ok = fill(&tmK, j + 1, hkv, it.b);
-            if (ok) ok = fill(&tmV, j, hkv, it.b);
+            if (j + 1 < it.nbmax) ok = fill(&tmK, j + 1, hkv, it.tb, it.s0);
+            if (ok) ok = fill(&tmV, j, hkv, it.tb, it.s0);
           }
         }
         // Let every load this thread issued land before the CTA exits (normally they were

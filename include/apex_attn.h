@@ -95,6 +95,44 @@ typedef struct apex_attn_fwd_args {
 int apex_attn_fwd_ex(const apex_attn_fwd_args* args, void* stream);
 
 /*
+ * Packed variable-length forward: the operation of apex_attn_fwd_ex on a batch of
+ * sequences of different lengths stored back to back (flash-attn's varlen layout).
+ *   q, o         [total, heads_q, D];   k, v  [total, heads_kv, D]
+ *   cu_seqlens   device int32 [batch + 1]: sequence b is rows [cu[b], cu[b+1]), cu[0] = 0,
+ *                nondecreasing, cu[batch] = total (the same offsets for q and k/v: packed
+ *                self-attention). Offsets are clamped to [0, total] and lengths to
+ *                max_seqlen on the device, so a malformed array gives wrong rows, never an
+ *                out-of-bounds access.
+ *   max_seqlen   the longest sequence (sizes the schedule; longer sequences are cut).
+ *   lse          nullable, fp32 [heads_q, total].
+ *   strides      8 values: (token, head) element strides of q, k, v, o.
+ * Rows of o outside every sequence are not written. Causal, window_left, GQA and sm_scale
+ * as for apex_attn_fwd_ex; the mask is relative to each sequence's first row.
+ * Has no counterpart in the reference operator (the GQA/varlen row of its next steps).
+ */
+typedef struct apex_attn_varlen_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse; /* nullable */
+  const int* cu_seqlens;
+  int batch;
+  int heads_q;
+  int heads_kv;
+  int total;
+  int max_seqlen;
+  int head_dim;
+  int dtype;
+  int causal;
+  int window_left;
+  float sm_scale;
+  long long strides[8];
+} apex_attn_varlen_args;
+
+int apex_attn_fwd_varlen(const apex_attn_varlen_args* args, void* stream);
+
+/*
  * Reads and clears the device status word of `device` after synchronising that
  * device. *flags receives the raw bits (1 = a kernel hit its bounded-wait limit,
  * 2 = a copy or MMA still in flight at kernel teardown did not land within the limit,

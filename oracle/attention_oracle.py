@@ -25,6 +25,8 @@ What it restates
   softmax(S) V, written out (P = softmax(S), dV = P^T dO, dP = dO V^T,
   dS = P * (dP - rowsum(dO * O)), dQ = scale dS K, dK = scale dS^T Q; grouped-query heads
   sum into their shared K/V head).
+* ``attention_varlen_np`` — ``attention_np`` per sequence of a packed variable-length
+  batch (flash-attn's varlen layout: rows cu_seqlens[b] .. cu_seqlens[b+1] - 1).
 * ``compute_flops`` — submission.py:235-240 (4*B*N^2*H*d, halved when causal).
 * ``make_inputs`` — the harness's seeded ``randn`` inputs (submission.py:278-287), drawn
   on the CPU generator in fp32 and rounded to the kernel dtype, so CPU and GPU see the
@@ -93,6 +95,27 @@ def attention_np(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool = Tru
             l = e.sum(axis=1, keepdims=True)
             o[b, h, r0:r1] = (e @ vh[:kmax]) / l
             lse[b, h, r0:r1] = (m + np.log(l))[:, 0]
+    return o, lse
+
+
+def attention_varlen_np(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_seqlens, causal: bool = True,
+                        sm_scale: float | None = None, window_left: int | None = None):
+    """attention_np over a packed batch: q [total, H, D], k, v [total, H_kv, D]; sequence b is
+    rows cu_seqlens[b] .. cu_seqlens[b+1] - 1 and attends only within itself.
+    Returns (o [total, H, D] float32, zero outside every sequence; lse [H, total] float32)."""
+    total, H, D = q.shape
+    o = np.zeros((total, H, D), dtype=np.float32)
+    lse = np.zeros((H, total), dtype=np.float32)
+    cu = [int(x) for x in cu_seqlens]
+    for b in range(len(cu) - 1):
+        a, e = cu[b], cu[b + 1]
+        if e <= a:
+            continue
+        seq = lambda t: np.ascontiguousarray(t[a:e].transpose(1, 0, 2))[None]
+        ob, lb = attention_np(seq(q), seq(k), seq(v), causal=causal, sm_scale=sm_scale,
+                              window_left=window_left)
+        o[a:e] = ob[0].transpose(1, 0, 2)
+        lse[:, a:e] = lb[0]
     return o, lse
 
 

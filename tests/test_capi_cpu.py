@@ -160,7 +160,8 @@ def _c_layout(struct: str, fields: list[str]) -> list[int]:
 
 
 @pytest.mark.parametrize("cls,struct", [(_lib.FwdArgs, "apex_attn_fwd_args"),
-                                        (_lib.BwdArgs, "apex_attn_bwd_args")])
+                                        (_lib.BwdArgs, "apex_attn_bwd_args"),
+                                        (_lib.VarlenArgs, "apex_attn_varlen_args")])
 def test_ctypes_structs_match_c_compiler_layout(cls, struct):
     import shutil
     if shutil.which("gcc") is None:
@@ -205,3 +206,39 @@ def test_bwd_workspace_checks(lib):
     assert lib.apex_attn_bwd(ctypes.byref(a), FAKE, need - 4, None) == _lib.ERR_INVALID_ARGUMENT
     assert lib.apex_attn_bwd(ctypes.byref(a), FAKE + 4, need, None) == _lib.ERR_BAD_LAYOUT
     assert lib.apex_attn_bwd(None, FAKE, need, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+# ----------------------------------------------------------------- varlen ----
+def _varlen_args(**kw):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, o=FAKE, lse=None, cu_seqlens=FAKE, batch=3, heads_q=4,
+             heads_kv=2, total=1000, max_seqlen=500, head_dim=128, dtype=0, causal=1,
+             window_left=-1, sm_scale=0.088)
+    strides = kw.pop("strides", [4 * 128, 128, 2 * 128, 128, 2 * 128, 128, 4 * 128, 128])
+    a.update(kw)
+    return _lib.VarlenArgs(strides=(ctypes.c_longlong * 8)(*strides), **a)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(cu_seqlens=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(q=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(batch=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(total=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(max_seqlen=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(heads_kv=3), _lib.ERR_INVALID_ARGUMENT),
+    (dict(window_left=5, causal=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(head_dim=96), _lib.ERR_UNSUPPORTED_HEAD_DIM),
+    (dict(dtype=9), _lib.ERR_UNSUPPORTED_DTYPE),
+    (dict(sm_scale=-1.0), _lib.ERR_BAD_SCALE),
+    (dict(strides=[4 * 128, 100, 256, 128, 256, 128, 512, 128]), _lib.ERR_BAD_LAYOUT),  # not x8
+    (dict(strides=[4 * 128, 64, 256, 128, 256, 128, 512, 128]), _lib.ERR_BAD_LAYOUT),   # head rows overlap
+    (dict(cu_seqlens=FAKE + 2), _lib.ERR_BAD_LAYOUT),
+    (dict(o=FAKE + 8), _lib.ERR_BAD_LAYOUT),
+    (dict(batch=1 << 28, max_seqlen=1 << 20), _lib.ERR_TOO_LARGE),
+])
+def test_varlen_argument_validation(lib, kw, code):
+    a = _varlen_args(**kw)
+    assert lib.apex_attn_fwd_varlen(ctypes.byref(a), None) == code
+
+
+def test_varlen_null_args(lib):
+    assert lib.apex_attn_fwd_varlen(None, None) == _lib.ERR_INVALID_ARGUMENT

@@ -164,3 +164,22 @@ def test_grad_close_bound():
     assert grad_close(e + np.array([0.009, 0.0, 0.0]), e)[0]
     assert not grad_close(e + np.array([0.011, 0.0, 0.0]), e)[0]
     assert grad_close(e + np.array([0.0, 0.0, 0.04]), e)[0]  # 1e-2 + 4 * 2^-7 = 0.041
+
+
+def test_varlen_oracle_is_per_sequence_attention():
+    from oracle.attention_oracle import attention_varlen_np
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((90, 4, 16)).astype(np.float32)
+    k = rng.standard_normal((90, 2, 16)).astype(np.float32)
+    v = rng.standard_normal((90, 2, 16)).astype(np.float32)
+    cu = [0, 30, 30, 31, 80]  # lengths 30, 0, 1, 49; rows 80..89 belong to no sequence
+    for causal, win in ((True, None), (False, None), (True, 7)):
+        o, lse = attention_varlen_np(q, k, v, cu, causal=causal, window_left=win)
+        assert not o[80:].any() and not lse[:, 80:].any()
+        for a, e in zip(cu[:-1], cu[1:]):
+            if e <= a:
+                continue
+            t = lambda x: x[a:e].transpose(1, 0, 2)[None]
+            ro, rl = attention_np(t(q), t(k), t(v), causal=causal, window_left=win)
+            np.testing.assert_allclose(o[a:e], ro[0].transpose(1, 0, 2), atol=1e-6)
+            np.testing.assert_allclose(lse[:, a:e], rl[0], atol=1e-6)
