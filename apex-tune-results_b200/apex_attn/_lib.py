@@ -64,6 +64,18 @@ class VarlenArgs(ctypes.Structure):
                 ("sm_scale", ctypes.c_float), ("strides", ctypes.c_longlong * 8)]
 
 
+class BwdVarlenArgs(ctypes.Structure):
+    """Mirror of apex_attn_bwd_varlen_args (include/apex_attn.h)."""
+    _fields_ = [("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+                ("o", ctypes.c_void_p), ("dout", ctypes.c_void_p), ("lse", ctypes.c_void_p),
+                ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p), ("dv", ctypes.c_void_p),
+                ("cu_seqlens", ctypes.c_void_p), ("batch", ctypes.c_int), ("heads_q", ctypes.c_int),
+                ("heads_kv", ctypes.c_int), ("total", ctypes.c_int), ("max_seqlen", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("dtype", ctypes.c_int), ("causal", ctypes.c_int),
+                ("window_left", ctypes.c_int), ("sm_scale", ctypes.c_float),
+                ("strides", ctypes.c_longlong * 16)]
+
+
 # Every symbol the header declares: (name, restype, argtypes).
 _c_ll_p = ctypes.POINTER(ctypes.c_longlong)
 SYMBOLS = {
@@ -84,6 +96,8 @@ SYMBOLS = {
     "apex_attn_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "apex_attn_bwd": (ctypes.c_int, [ctypes.POINTER(BwdArgs), ctypes.c_void_p, ctypes.c_size_t,
                                      ctypes.c_void_p]),
+    "apex_attn_bwd_varlen": (ctypes.c_int, [ctypes.POINTER(BwdVarlenArgs), ctypes.c_void_p,
+                                            ctypes.c_size_t, ctypes.c_void_p]),
     "apex_attn_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "apex_attn_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p]),
     "apex_attn_strerror": (ctypes.c_char_p, [ctypes.c_int]),

@@ -214,6 +214,66 @@ def custom_attention_backward(q, k, v, o, lse, dout, causal=True, sm_scale=None,
     return dq, dk, dv
 
 
+def custom_attention_varlen_backward(q, k, v, o, lse, dout, cu_seqlens, max_seqlen, causal=True,
+                                     sm_scale=None, window_left=None):
+    """Gradients (dq, dk, dv) of custom_attention_varlen_forward: packed q, o, dout
+    [total, H, D], k, v [total, H_kv, D], lse fp32 [H, total] from the forward, cu_seqlens and
+    max_seqlen as for the forward. Head dims 64 and 128. Rows outside every sequence come
+    back as zeros. Deterministic; asynchronous on the current stream.
+    """
+    if q.dim() != 3 or k.shape != v.shape or o.shape != q.shape or dout.shape != q.shape:
+        raise ValueError("expected q, o, dout [total, H, D] and k, v [total, H_kv, D]")
+    total, nheads, headdim = q.shape
+    kv_heads = k.shape[1]
+    if (k.shape[0], k.shape[2]) != (total, headdim) or nheads % kv_heads != 0:
+        raise ValueError("k and v must be [total, H_kv, D] with H_kv dividing q's heads")
+    if headdim not in (64, 128):
+        raise KeyError(headdim)
+    if q.dtype not in _DTYPES or any(t.dtype != q.dtype for t in (k, v, o, dout)):
+        raise TypeError("q, k, v, o, dout must share one dtype, float16 or bfloat16")
+    if lse.shape != (nheads, total) or lse.dtype != torch.float32:
+        raise ValueError(f"lse must be float32 [H, total], got {lse.dtype} {tuple(lse.shape)}")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.dim() != 1 or cu_seqlens.numel() < 2:
+        raise ValueError("cu_seqlens must be a 1-D int32 tensor of batch + 1 offsets")
+    if not all(t.is_cuda and t.device == q.device for t in (q, k, v, o, dout, lse, cu_seqlens)):
+        raise ValueError("all tensors must be CUDA tensors on one device")
+    if window_left is not None and (window_left < 0 or not causal):
+        raise ValueError("window_left must be >= 0 and needs causal=True")
+
+    def ready(t):
+        if t.stride(-1) != 1 or t.data_ptr() % 16 != 0 or any(s % 8 for s in t.stride()[:2]):
+            return t.contiguous()
+        return t
+    q, k, v, o, dout = (ready(t) for t in (q, k, v, o, dout))
+    lse, cu_seqlens = lse.contiguous(), cu_seqlens.contiguous()
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(headdim)
+    dq = torch.zeros(q.shape, dtype=q.dtype, device=q.device)
+    dk = torch.zeros(k.shape, dtype=q.dtype, device=q.device)
+    dv = torch.zeros(k.shape, dtype=q.dtype, device=q.device)
+    if total == 0:
+        return dq, dk, dv
+    batch = cu_seqlens.numel() - 1
+    lib = _lib.load()
+    ws_bytes = int(lib.apex_attn_bwd_workspace_bytes(batch, nheads, int(max_seqlen)))
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    strides = []
+    for t in (q, k, v, o, dout, dq, dk, dv):
+        strides += [t.stride(0), t.stride(1)]
+    args = _lib.BwdVarlenArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), o=o.data_ptr(),
+                              dout=dout.data_ptr(), lse=lse.data_ptr(), dq=dq.data_ptr(),
+                              dk=dk.data_ptr(), dv=dv.data_ptr(), cu_seqlens=cu_seqlens.data_ptr(),
+                              batch=batch, heads_q=nheads, heads_kv=kv_heads, total=total,
+                              max_seqlen=int(max_seqlen), head_dim=headdim, dtype=_DTYPES[q.dtype],
+                              causal=1 if causal else 0,
+                              window_left=-1 if window_left is None else int(window_left),
+                              sm_scale=float(sm_scale), strides=(ctypes.c_longlong * 16)(*strides))
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = lib.apex_attn_bwd_varlen(ctypes.byref(args), workspace.data_ptr(), ws_bytes, stream)
+    _lib.check(rc, "custom_attention_varlen_backward")
+    return dq, dk, dv
+
+
 def device_status(device: int | None = None) -> int:
     """Synchronises `device`, returns and clears its status bits (0 = no kernel fault)."""
     if device is None:

@@ -82,6 +82,12 @@ struct BwdParams {
   float out1_scale;      // sm_scale (dK = scale dS^T Q, dQ = scale dS K)
   int causal;
   int window;            // -1: none
+  // Packed variable-length batch (VAR kernels): sequence b is rows
+  // [cu_seqlens[b], cu_seqlens[b + 1]) of tensors with `total` rows, N is the longest
+  // sequence; the statistics stay [B][H][Npad] (per sequence, padded). Offsets are
+  // clamped to [0, total] and lengths to N on the device.
+  const int* cu_seqlens;
+  int total;
   unsigned long long timeout_ns;
 };
 
@@ -161,11 +167,12 @@ struct BwdSmem {
 // query head in the Q pass) and the range [lo, hi) of streaming tiles it meets (query tiles
 // in the KV pass, repeated for each of the kv_group query heads; key blocks in the Q pass).
 struct BwdItem {
-  int b, hx, blk, lo, hi, nsteps;
+  int b, hx, blk, lo, hi, nsteps;  // nsteps = 0: a block past its sequence's end (packed batch)
+  int s0, len, tb;  // first row of the sequence in the tensors, its length, TMA batch coordinate
 };
 
 // Item t -> work, longest first inside equal-size L2 groups of heads (see decode_item).
-template <bool KV, bool WIN>
+template <bool KV, bool WIN, bool VAR>
 __device__ __forceinline__ BwdItem decode_bwd(int t, const BwdParams& p) {
   const int MB = p.nblk;
   const int q = p.group_q;
@@ -189,19 +196,33 @@ __device__ __forceinline__ BwdItem decode_bwd(int t, const BwdParams& p) {
   BwdItem it;
   it.b = bh / HX;
   it.hx = bh - it.b * HX;
+  int nblk = p.nblk;  // 128-row blocks of this item's sequence
+  if (VAR) {
+    const int a = min(max(__ldg(p.cu_seqlens + it.b), 0), p.total);
+    const int e = min(max(__ldg(p.cu_seqlens + it.b + 1), a), p.total);
+    it.s0 = a;
+    it.len = min(e - a, p.N);
+    it.tb = 0;
+    nblk = (it.len + kBlockM - 1) / kBlockM;
+  } else {
+    it.s0 = 0;
+    it.len = p.N;
+    it.tb = it.b;
+  }
   if (KV) {
     // Causal: key block blk is seen by query tiles >= blk, so low blocks are the long ones.
     it.blk = rb;
     it.lo = p.causal ? it.blk : 0;
-    it.hi = p.nblk;
-    if (WIN) it.hi = min(p.nblk, (it.blk * kBlockN + kBlockN - 1 + p.window) / kBlockM + 1);
+    it.hi = nblk;
+    if (WIN) it.hi = min(nblk, (it.blk * kBlockN + kBlockN - 1 + p.window) / kBlockM + 1);
     it.nsteps = p.kv_group * (it.hi - it.lo);
   } else {
     it.blk = MB - 1 - rb;
     it.lo = WIN ? max(0, it.blk * kBlockM - p.window) / kBlockN : 0;
-    it.hi = p.causal ? it.blk + 1 : p.nblk;
+    it.hi = p.causal ? it.blk + 1 : nblk;
     it.nsteps = it.hi - it.lo;
   }
+  if (it.blk >= nblk) it.nsteps = 0;
   return it;
 }
 
@@ -209,7 +230,7 @@ __device__ __forceinline__ BwdItem decode_bwd(int t, const BwdParams& p) {
 // for i < Npad (padding rows: ndelta 0, nlse2 -inf), stored negated so the elementwise
 // warps add them with one packed instruction. kTpr = D / 8 threads per row, each reading
 // one 16-byte vector of O and of dO.
-template <typename T, int D>
+template <typename T, int D, bool VAR>
 __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const T* __restrict__ o,
                                                             const T* __restrict__ dout,
                                                             const float* __restrict__ lse,
@@ -218,7 +239,8 @@ __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const T* __restrict_
                                                             long long o_sh, long long o_sn,
                                                             long long d_sb, long long d_sh,
                                                             long long d_sn, int H, int N, int Npad,
-                                                            long long rows) {
+                                                            long long rows, const int* cu_seqlens,
+                                                            int total) {
   constexpr int kTpr = D / 8;
   const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / kTpr;
   const int sub = (int)(threadIdx.x % kTpr);
@@ -227,10 +249,20 @@ __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const T* __restrict_
   const long long bh = in_range ? row / Npad : 0;
   const int b = (int)(bh / H);
   const int h = (int)(bh - (long long)b * H);
+  // Row i of sequence b: tensor row s0 + i (packed batch) or row i of batch b.
+  int len = N;
+  long long s0 = 0;
+  if (VAR && in_range) {
+    const int a0 = min(max(__ldg(cu_seqlens + b), 0), total);
+    const int e0 = min(max(__ldg(cu_seqlens + b + 1), a0), total);
+    s0 = a0;
+    len = min(e0 - a0, N);
+  }
+  const long long ob = VAR ? 0 : (long long)b * o_sb, db = VAR ? 0 : (long long)b * d_sb;
   float acc = 0.f;
-  if (in_range && i < N) {
-    const uint4 a = *reinterpret_cast<const uint4*>(o + b * o_sb + h * o_sh + i * o_sn + sub * 8);
-    const uint4 g = *reinterpret_cast<const uint4*>(dout + b * d_sb + h * d_sh + i * d_sn + sub * 8);
+  if (in_range && i < len) {
+    const uint4 a = *reinterpret_cast<const uint4*>(o + ob + h * o_sh + (s0 + i) * o_sn + sub * 8);
+    const uint4 g = *reinterpret_cast<const uint4*>(dout + db + h * d_sh + (s0 + i) * d_sn + sub * 8);
     const T* av = reinterpret_cast<const T*>(&a);
     const T* gv = reinterpret_cast<const T*>(&g);
 #pragma unroll
@@ -240,12 +272,15 @@ __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const T* __restrict_
   for (int w = kTpr / 2; w > 0; w >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, w);
   if (in_range && sub == 0) {
     ndelta[row] = -acc;
-    nlse2[row] = i < N ? lse[bh * N + i] * -1.4426950408889634f : -INFINITY;
+    // lse: [B, H, N]; packed batch: [H, total]
+    const long long li = VAR ? (long long)h * total + s0 + i : bh * N + i;
+    nlse2[row] = i < len ? lse[li] * -1.4426950408889634f : -INFINITY;
   }
 }
 
-// KV = true: dK, dV pass; KV = false: dQ pass. WIN: causal sliding window in use.
-template <int D, typename T, bool KV, bool WIN>
+// KV = true: dK, dV pass; KV = false: dQ pass. WIN: causal sliding window in use. VAR:
+// packed variable-length batch.
+template <int D, typename T, bool KV, bool WIN, bool VAR>
 __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmX1,
                           const __grid_constant__ CUtensorMap tmX2,
@@ -337,7 +372,8 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     while (ok) {
       int t;
       if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-      const BwdItem it = decode_bwd<KV, WIN>(t, p);
+      const BwdItem it = decode_bwd<KV, WIN, VAR>(t, p);
+      if (it.nsteps == 0) continue;  // block past its sequence's end: no work, no barrier
       const int nq = it.hi - it.lo;
       float row_nlse2 = 0.f, row_ndelta = 0.f;
       if (!KV) {
@@ -386,7 +422,10 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         const int it_q = KV ? ytile : it.blk;
         const int jb_k = KV ? it.blk : ytile;
         const int dq0 = (it_q - jb_k) * kBlockM;
-        const bool masked = (p.causal && it_q == jb_k) || (WIN && dq0 + kBlockM - 1 > p.window);
+        // Packed batch, Q pass, full attention: keys past the sequence end belong to the next
+        // sequence (not zero-filled) and are masked.
+        const bool key_tail = VAR && !KV && !p.causal && (ytile + 1) * kBlockN > it.len;
+        const bool masked = (p.causal && it_q == jb_k) || (WIN && dq0 + kBlockM - 1 > p.window) || key_tail;
         const int colbase = 64 * half;
         if (!(ok = W.wait_warp(bar(Plan::kT1Full), t1_par))) break;
         t1_par ^= 1;
@@ -430,7 +469,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 64; ++e) {
             const int dqk = dq0 + (KV ? colbase + e - r : r - colbase - e);
-            if ((p.causal && dqk < 0) || (WIN && dqk > p.window)) pv[e] = -INFINITY;
+            if ((p.causal && dqk < 0) || (WIN && dqk > p.window) ||
+                (key_tail && ytile * kBlockN + colbase + e >= it.len))
+              pv[e] = -INFINITY;
           }
         }
         if (masked || kEmu == 0) {
@@ -504,11 +545,11 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       af_par ^= 1;
       ptx::tc_fence_after();
       const int row = it.blk * kBlockM + r;
-      const bool valid = row < p.N;
+      const bool valid = row < it.len;
       constexpr int kHalfCols = D / 2;
       auto store = [&](void* base, long long sb, long long sh, long long sn, int acc_col, float scale) {
-        T* dst = reinterpret_cast<T*>(base) + (long long)it.b * sb + (long long)it.hx * sh +
-                 (long long)row * sn + half * kHalfCols;
+        T* dst = reinterpret_cast<T*>(base) + (VAR ? 0LL : (long long)it.b * sb) + (long long)it.hx * sh +
+                 (long long)(it.s0 + row) * sn + half * kHalfCols;
 #pragma unroll 1
         for (int ch = 0; ch < kHalfCols / 32; ++ch) {
           uint32_t v[32];
@@ -629,7 +670,8 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     while (ok) {
       int t;
       if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-      const BwdItem it = decode_bwd<KV, WIN>(t, p);
+      const BwdItem it = decode_bwd<KV, WIN, VAR>(t, p);
+      if (it.nsteps == 0) continue;  // block past its sequence's end
       // Q pass: the elementwise warps copy the next item's X only after finishing this
       // item's epilogue, which waits for the last A(); issue it before waiting for X.
       if (!KV && pend.valid) {
@@ -728,12 +770,13 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         ptx::mbar_arrive(bar(Plan::kItemFull + slot));
         ++published;
         if (t < 0) break;
-        const BwdItem it = decode_bwd<KV, WIN>(t, p);
+        const BwdItem it = decode_bwd<KV, WIN, VAR>(t, p);
+        if (it.nsteps == 0) continue;  // block past its sequence's end
         if (!(ok = W.wait(bar(Plan::kXEmpty), xe_par))) break;
         xe_par ^= 1;
         ptx::mbar_arrive_expect_tx(bar(Plan::kXFull), 2u * Plan::kTileBytes);
-        load_tile(sX1, &tmX1, bar(Plan::kXFull), it.blk * kBlockM, it.hx, it.b, pol_x);
-        load_tile(sX2, &tmX2, bar(Plan::kXFull), it.blk * kBlockM, it.hx, it.b, pol_x);
+        load_tile(sX1, &tmX1, bar(Plan::kXFull), it.s0 + it.blk * kBlockM, it.hx, it.tb, pol_x);
+        load_tile(sX2, &tmX2, bar(Plan::kXFull), it.s0 + it.blk * kBlockM, it.hx, it.tb, pol_x);
         ++x_fills;
         const int nq = it.hi - it.lo;
         for (int s = 0; s < it.nsteps && ok; ++s) {
@@ -746,7 +789,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             if (!(ok = W.wait(bar(Plan::kRingEmpty + st), ph ^ 1))) break;
             ptx::mbar_arrive_expect_tx(bar(Plan::kRingFull + st), (uint32_t)Plan::kTileBytes);
             load_tile(sRing + st * Plan::kTileBytes, k == 0 ? &tmY1 : &tmY2, bar(Plan::kRingFull + st),
-                      ytile * kBlockN, hy, it.b, pol_y);
+                      it.s0 + ytile * kBlockN, hy, it.tb, pol_y);
             ++fills;
           }
           if (KV && ok) {

@@ -468,12 +468,26 @@ size_t bwd_workspace_bytes(int batch, int heads_q, int seqlen) {
   return (size_t)2 * (size_t)batch * (size_t)heads_q * (size_t)bwd_padded_rows(seqlen) * sizeof(float);
 }
 
-template <int D, typename T, bool KV, bool WIN>
+// The backward's inputs in one shape for the batched and the packed entry points: strides
+// are (batch, head, row) element strides of q, k, v, o, dout, dq, dk, dv (batch stride 0
+// for a packed batch, whose rows are tokens).
+struct BwdCall {
+  const void *o, *dout;
+  const float* lse;
+  void *dq, *dk, *dv;
+  int batch, heads_q, heads_kv, seqlen, causal, window_left;  // seqlen: the longest sequence
+  float sm_scale;
+  long long st[24];
+  const int* cu_seqlens;  // null: batched
+  int total;
+};
+
+template <int D, typename T, bool KV, bool WIN, bool VAR>
 int launch_bwd_one(DeviceState& ds, const CUtensorMap& x1, const CUtensorMap& x2, const CUtensorMap& y1,
                    const CUtensorMap& y2, const apex::BwdParams& p, int grid, cudaStream_t stream) {
-  auto kern = apex::attn_bwd_sm100_kernel<D, T, KV, WIN>;
+  auto kern = apex::attn_bwd_sm100_kernel<D, T, KV, WIN, VAR>;
   constexpr int smem = apex::BwdSmem<D>::kDynamicBytes;
-  constexpr unsigned bit = 1u << ((D == 128 ? 8 : 0) + (std::is_same<T, __half>::value ? 4 : 0) +
+  constexpr unsigned bit = 1u << ((VAR ? 16 : 0) + (D == 128 ? 8 : 0) + (std::is_same<T, __half>::value ? 4 : 0) +
                                   (KV ? 2 : 0) + (WIN ? 1 : 0));
   if (!(ds.attr_bwd & bit)) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -488,17 +502,33 @@ int launch_bwd_one(DeviceState& ds, const CUtensorMap& x1, const CUtensorMap& x2
   return APEX_ATTN_OK;
 }
 
+// Both passes of one direction (dK/dV or dQ), windowed or not.
+template <int D, typename T, bool KV, bool VAR>
+int launch_bwd_pass(DeviceState& ds, bool win, const CUtensorMap& x1, const CUtensorMap& x2,
+                    const CUtensorMap& y1, const CUtensorMap& y2, const apex::BwdParams& p, int grid,
+                    cudaStream_t s) {
+  return win ? launch_bwd_one<D, T, KV, true, VAR>(ds, x1, x2, y1, y2, p, grid, s)
+             : launch_bwd_one<D, T, KV, false, VAR>(ds, x1, x2, y1, y2, p, grid, s);
+}
+
 // Prep pass, then the dK/dV pass (K, V stationary) and the dQ pass (Q, dO stationary).
 template <int D, typename T>
-int launch_bwd(DeviceState& ds, const apex_attn_bwd_args& a, const CUtensorMap& mq, const CUtensorMap& mk,
+int launch_bwd(DeviceState& ds, const BwdCall& a, const CUtensorMap& mq, const CUtensorMap& mk,
                const CUtensorMap& mv, const CUtensorMap& mdo, float* lse2, float* delta, cudaStream_t s) {
-  const long long* st = a.strides;
+  const long long* st = a.st;
+  const bool var = a.cu_seqlens != nullptr;
   const int npad = (int)bwd_padded_rows(a.seqlen);
   const long long rows = (long long)a.batch * a.heads_q * npad;
   const long long threads = rows * (D / 8);
-  apex::attn_bwd_prep_kernel<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
-      static_cast<const T*>(a.o), static_cast<const T*>(a.dout), a.lse, lse2, delta, st[9], st[10], st[11],
-      st[12], st[13], st[14], a.heads_q, a.seqlen, npad, rows);
+  const unsigned blocks = (unsigned)((threads + 255) / 256);
+  if (var)
+    apex::attn_bwd_prep_kernel<T, D, true><<<blocks, 256, 0, s>>>(
+        static_cast<const T*>(a.o), static_cast<const T*>(a.dout), a.lse, lse2, delta, st[9], st[10], st[11],
+        st[12], st[13], st[14], a.heads_q, a.seqlen, npad, rows, a.cu_seqlens, a.total);
+  else
+    apex::attn_bwd_prep_kernel<T, D, false><<<blocks, 256, 0, s>>>(
+        static_cast<const T*>(a.o), static_cast<const T*>(a.dout), a.lse, lse2, delta, st[9], st[10], st[11],
+        st[12], st[13], st[14], a.heads_q, a.seqlen, npad, rows, nullptr, 0);
   if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
 
   apex::BwdParams p{};
@@ -518,6 +548,8 @@ int launch_bwd(DeviceState& ds, const apex_attn_bwd_args& a, const CUtensorMap& 
   // A window of seqlen or more hides nothing: run the plain causal kernels (this also keeps
   // the kernels' window arithmetic far from int overflow).
   p.window = a.window_left < a.seqlen ? a.window_left : -1;
+  p.cu_seqlens = a.cu_seqlens;
+  p.total = a.total;
   p.timeout_ns = wait_timeout_ns();
   // L2 groups as in the forward: the streamed tiles of the heads that concurrently running
   // CTAs walk should stay within ~48 MB of L2.
@@ -544,8 +576,8 @@ int launch_bwd(DeviceState& ds, const apex_attn_bwd_args& a, const CUtensorMap& 
     return APEX_ATTN_ERR_CUDA;
   }
   const int grid_kv = std::min(pk.num_items, ds.num_sms);
-  rc = win ? launch_bwd_one<D, T, true, true>(ds, mk, mv, mq, mdo, pk, grid_kv, s)
-           : launch_bwd_one<D, T, true, false>(ds, mk, mv, mq, mdo, pk, grid_kv, s);
+  rc = var ? launch_bwd_pass<D, T, true, true>(ds, win, mk, mv, mq, mdo, pk, grid_kv, s)
+           : launch_bwd_pass<D, T, true, false>(ds, win, mk, mv, mq, mdo, pk, grid_kv, s);
   if (rc != APEX_ATTN_OK) return rc;
   // dQ: items over (batch, query head, query block); K and V stream.
   apex::BwdParams pq = p;
@@ -558,9 +590,13 @@ int launch_bwd(DeviceState& ds, const apex_attn_bwd_args& a, const CUtensorMap& 
     return APEX_ATTN_ERR_CUDA;
   }
   const int grid_q = std::min(pq.num_items, ds.num_sms);
-  return win ? launch_bwd_one<D, T, false, true>(ds, mq, mdo, mk, mv, pq, grid_q, s)
-             : launch_bwd_one<D, T, false, false>(ds, mq, mdo, mk, mv, pq, grid_q, s);
+  return var ? launch_bwd_pass<D, T, false, true>(ds, win, mq, mdo, mk, mv, pq, grid_q, s)
+             : launch_bwd_pass<D, T, false, false>(ds, win, mq, mdo, mk, mv, pq, grid_q, s);
 }
+
+int dispatch_bwd(DeviceState& ds, const BwdCall& call, int head_dim, int dtype, const CUtensorMap& mq,
+                 const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo, void* workspace,
+                 long long npad, void* stream);
 
 int backward(const apex_attn_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream) {
   // ---- argument validation (no CUDA calls) ----
@@ -606,15 +642,84 @@ int backward(const apex_attn_bwd_args* a, void* workspace, size_t workspace_byte
       (rc = encode_map(&mv, a->v, a->dtype, B, HKV, N, D, st[6], st[7], st[8])) ||
       (rc = encode_map(&mdo, a->dout, a->dtype, B, H, N, D, st[12], st[13], st[14])))
     return rc;
+  BwdCall call{a->o, a->dout, a->lse, a->dq, a->dk, a->dv, B, H, HKV, N, a->causal, a->window_left,
+               a->sm_scale, {}, nullptr, 0};
+  for (int i = 0; i < 24; ++i) call.st[i] = st[i];
+  return dispatch_bwd(*ds, call, a->head_dim, a->dtype, mq, mk, mv, mdo, workspace, npad, stream);
+}
+
+int dispatch_bwd(DeviceState& ds, const BwdCall& call, int head_dim, int dtype, const CUtensorMap& mq,
+                 const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo, void* workspace,
+                 long long npad, void* stream) {
   float* lse2 = static_cast<float*>(workspace);
-  float* delta = lse2 + (size_t)B * H * npad;
+  float* delta = lse2 + (size_t)call.batch * call.heads_q * npad;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool bf16 = a->dtype == APEX_ATTN_BF16;
-  if (D == 64)
-    return bf16 ? launch_bwd<64, __nv_bfloat16>(*ds, *a, mq, mk, mv, mdo, lse2, delta, s)
-                : launch_bwd<64, __half>(*ds, *a, mq, mk, mv, mdo, lse2, delta, s);
-  return bf16 ? launch_bwd<128, __nv_bfloat16>(*ds, *a, mq, mk, mv, mdo, lse2, delta, s)
-              : launch_bwd<128, __half>(*ds, *a, mq, mk, mv, mdo, lse2, delta, s);
+  const bool bf16 = dtype == APEX_ATTN_BF16;
+  if (head_dim == 64)
+    return bf16 ? launch_bwd<64, __nv_bfloat16>(ds, call, mq, mk, mv, mdo, lse2, delta, s)
+                : launch_bwd<64, __half>(ds, call, mq, mk, mv, mdo, lse2, delta, s);
+  return bf16 ? launch_bwd<128, __nv_bfloat16>(ds, call, mq, mk, mv, mdo, lse2, delta, s)
+              : launch_bwd<128, __half>(ds, call, mq, mk, mv, mdo, lse2, delta, s);
+}
+
+// Packed variable-length backward (apex_attn_bwd_varlen).
+int backward_varlen(const apex_attn_bwd_varlen_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+  // ---- argument validation (no CUDA calls) ----
+  if (!a) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv ||
+      !a->cu_seqlens || !workspace)
+    return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->batch <= 0 || a->heads_q <= 0 || a->total <= 0 || a->max_seqlen <= 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->heads_kv <= 0 || a->heads_q % a->heads_kv != 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->window_left < -1 || (a->window_left >= 0 && !a->causal)) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (a->head_dim != 64 && a->head_dim != 128) return APEX_ATTN_ERR_UNSUPPORTED_HEAD_DIM;
+  if (a->dtype != APEX_ATTN_BF16 && a->dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
+  if (!std::isfinite(a->sm_scale) || !(a->sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
+  const long long npad = bwd_padded_rows(a->max_seqlen);
+  if ((long long)a->batch * a->heads_q * (npad / kBwdBlock) > 0x7fffffffLL || a->total > (1 << 30) ||
+      a->max_seqlen > (1 << 30) || (long long)a->batch * a->heads_q * npad > (1LL << 40))
+    return APEX_ATTN_ERR_TOO_LARGE;
+  for (int i = 0; i < 16; ++i)
+    if (a->strides[i] < 0 || (a->strides[i] & 7) != 0 || a->strides[i] >= (1LL << 38)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  for (int t = 0; t < 8; ++t)
+    if (a->strides[2 * t + 1] < a->head_dim) return APEX_ATTN_ERR_BAD_LAYOUT;
+  const void* ptrs[8] = {a->q, a->k, a->v, a->o, a->dout, a->dq, a->dk, a->dv};
+  for (const void* ptr : ptrs)
+    if (!aligned16(ptr)) return APEX_ATTN_ERR_BAD_LAYOUT;
+  if ((reinterpret_cast<uintptr_t>(a->lse) & 3u) || (reinterpret_cast<uintptr_t>(a->cu_seqlens) & 3u) ||
+      !aligned16(workspace))
+    return APEX_ATTN_ERR_BAD_LAYOUT;
+  if (workspace_bytes < bwd_workspace_bytes(a->batch, a->heads_q, a->max_seqlen)) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+
+  // ---- device ----
+  const int dev = device_of(a->q);
+  if (dev < 0) return APEX_ATTN_ERR_NO_DEVICE;
+  for (const void* ptr : ptrs)
+    if (device_of(ptr) != dev) return APEX_ATTN_ERR_NO_DEVICE;
+  if (device_of(a->lse) != dev || device_of(a->cu_seqlens) != dev || device_of(workspace) != dev)
+    return APEX_ATTN_ERR_NO_DEVICE;
+  DeviceGuard guard(dev);
+  DeviceState* ds = nullptr;
+  int rc = init_device(dev, &ds);
+  if (rc != APEX_ATTN_OK) return rc;
+
+  // Tensor maps over the packed rows: dims (D, total, H, 1); strides are (token, head).
+  const long long* st = a->strides;
+  const int T = a->total, D = a->head_dim;
+  CUtensorMap mq, mk, mv, mdo;
+  if ((rc = encode_map(&mq, a->q, a->dtype, 1, a->heads_q, T, D, 0, st[1], st[0])) ||
+      (rc = encode_map(&mk, a->k, a->dtype, 1, a->heads_kv, T, D, 0, st[3], st[2])) ||
+      (rc = encode_map(&mv, a->v, a->dtype, 1, a->heads_kv, T, D, 0, st[5], st[4])) ||
+      (rc = encode_map(&mdo, a->dout, a->dtype, 1, a->heads_q, T, D, 0, st[9], st[8])))
+    return rc;
+  BwdCall call{a->o, a->dout, a->lse, a->dq, a->dk, a->dv, a->batch, a->heads_q, a->heads_kv,
+               a->max_seqlen, a->causal, a->window_left, a->sm_scale, {}, a->cu_seqlens, a->total};
+  for (int t = 0; t < 8; ++t) {  // (batch, head, row) per tensor; no batch stride when packed
+    call.st[3 * t] = 0;
+    call.st[3 * t + 1] = st[2 * t + 1];
+    call.st[3 * t + 2] = st[2 * t];
+  }
+  return dispatch_bwd(*ds, call, a->head_dim, a->dtype, mq, mk, mv, mdo, workspace, npad, stream);
 }
 
 }  // namespace
@@ -627,6 +732,11 @@ size_t apex_attn_bwd_workspace_bytes(int batch, int heads_q, int seqlen) {
 
 int apex_attn_bwd(const apex_attn_bwd_args* args, void* workspace, size_t workspace_bytes, void* stream) {
   return backward(args, workspace, workspace_bytes, stream);
+}
+
+int apex_attn_bwd_varlen(const apex_attn_bwd_varlen_args* args, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  return backward_varlen(args, workspace, workspace_bytes, stream);
 }
 
 int apex_attn_version(void) { return kVersion; }

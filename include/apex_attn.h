@@ -226,6 +226,43 @@ size_t apex_attn_bwd_workspace_bytes(int batch, int heads_q, int seqlen);
 int apex_attn_bwd(const apex_attn_bwd_args* args, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/*
+ * Backward of apex_attn_fwd_varlen: dq, dk, dv of a packed variable-length batch.
+ *   q, o, dout, dq   [total, heads_q, D];   k, v, dk, dv   [total, heads_kv, D]
+ *   lse              fp32 [heads_q, total], as apex_attn_fwd_varlen writes it
+ *   cu_seqlens, max_seqlen, causal, window_left, sm_scale: as for apex_attn_fwd_varlen
+ *   strides          16 values: (token, head) element strides of q, k, v, o, dout, dq, dk, dv
+ *   workspace        apex_attn_bwd_workspace_bytes(batch, heads_q, max_seqlen) bytes
+ * Rows outside every sequence are not written. Offsets are clamped on the device as for
+ * the forward. Head dims 64 and 128. No counterpart in the reference operator.
+ */
+typedef struct apex_attn_bwd_varlen_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  const float* lse;
+  void* dq;
+  void* dk;
+  void* dv;
+  const int* cu_seqlens;
+  int batch;
+  int heads_q;
+  int heads_kv;
+  int total;
+  int max_seqlen;
+  int head_dim;
+  int dtype;
+  int causal;
+  int window_left;
+  float sm_scale;
+  long long strides[16];
+} apex_attn_bwd_varlen_args;
+
+int apex_attn_bwd_varlen(const apex_attn_bwd_varlen_args* args, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Human-readable text for a status code. Replaces the exception text the reference
  * harness prints on failure (submission.py:299-306). */
 const char* apex_attn_strerror(int status);

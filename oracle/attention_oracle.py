@@ -168,6 +168,27 @@ def attention_bwd_np(q: np.ndarray, k: np.ndarray, v: np.ndarray, do: np.ndarray
     return dq.astype(np.float32), dk.astype(np.float32), dv.astype(np.float32)
 
 
+def attention_varlen_bwd_np(q, k, v, do, cu_seqlens, causal: bool = True, sm_scale: float | None = None,
+                            window_left: int | None = None):
+    """attention_bwd_np per sequence of a packed batch (layout of attention_varlen_np).
+    Returns (dq [total, H, D], dk, dv [total, H_kv, D]) float32, zero outside every sequence."""
+    dq = np.zeros(q.shape, dtype=np.float32)
+    dk = np.zeros(k.shape, dtype=np.float32)
+    dv = np.zeros(k.shape, dtype=np.float32)
+    cu = [int(x) for x in cu_seqlens]
+    for b in range(len(cu) - 1):
+        a, e = cu[b], cu[b + 1]
+        if e <= a:
+            continue
+        seq = lambda t: np.ascontiguousarray(t[a:e].transpose(1, 0, 2))[None]
+        gq, gk, gv = attention_bwd_np(seq(q), seq(k), seq(v), seq(do), causal=causal, sm_scale=sm_scale,
+                                      window_left=window_left)
+        dq[a:e] = gq[0].transpose(1, 0, 2)
+        dk[a:e] = gk[0].transpose(1, 0, 2)
+        dv[a:e] = gv[0].transpose(1, 0, 2)
+    return dq, dk, dv
+
+
 def grad_close(actual: np.ndarray, expected: np.ndarray, atol: float = 1e-2,
                rtol: float = 2.0 ** -7) -> tuple[bool, float]:
     """Tolerance of the 16-bit backward: |a - e| <= atol + rtol |e| elementwise.

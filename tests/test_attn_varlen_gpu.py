@@ -126,3 +126,71 @@ def test_malformed_offsets_stay_in_bounds():
     assert torch.isfinite(o.float()).all()
     assert (o[total:] == 7.0).all()
     assert not (o[:256] == 7.0).all()  # the first sequence (cut to 256 rows) was written
+
+
+# ---------------------------------------------------------------- backward --
+from oracle.attention_oracle import attention_varlen_bwd_np, grad_close  # noqa: E402
+
+BWD_CASES = [
+    # lens, H, HKV, D, causal, window, dtype
+    ([300, 1, 128, 129, 700], 2, 2, 128, True, None, "bfloat16"),
+    ([300, 1, 128, 129, 700], 2, 2, 128, False, None, "bfloat16"),
+    ([64, 0, 500, 17], 4, 1, 64, True, None, "bfloat16"),
+    ([1000, 255, 256, 257], 2, 2, 64, False, None, "bfloat16"),
+    ([640, 130, 900], 4, 2, 128, True, 100, "bfloat16"),
+    ([384, 96, 512], 2, 2, 64, True, None, "float16"),
+]
+
+
+@pytest.mark.parametrize("lens,H,HKV,D,causal,win,dtype", BWD_CASES)
+def test_varlen_backward_vs_oracle(lens, H, HKV, D, causal, win, dtype):
+    """Backward given the oracle's o and lse; tolerance of the batched backward parity
+    (1e-2 + 2^-7 |ref|)."""
+    from apex_attn import custom_attention_varlen_backward
+    from oracle.attention_oracle import attention_varlen_np
+    q, k, v, cu = packed_inputs(lens, H, HKV, D, dtype, seed=sum(lens) + 7 * D)
+    g = torch.Generator().manual_seed(1)
+    do = torch.randn(q.shape, generator=g).to(q.dtype)
+    f32 = [t.float().numpy() for t in (q, k, v, do)]
+    o, lse = attention_varlen_np(*f32[:3], cu, causal=causal, window_left=win)
+    got = custom_attention_varlen_backward(
+        q.cuda(), k.cuda(), v.cuda(), torch.from_numpy(o).to(q.dtype).cuda(), torch.from_numpy(lse).cuda(),
+        do.cuda(), torch.from_numpy(cu).cuda(), max(lens), causal=causal, window_left=win)
+    torch.cuda.synchronize()
+    ref = attention_varlen_bwd_np(*f32, cu, causal=causal, window_left=win)
+    for name, a, r in zip(("dq", "dk", "dv"), got, ref):
+        ok, ratio = grad_close(a.float().cpu().numpy(), r)
+        assert ok, f"lens={lens} D={D} causal={causal} win={win} {name}: err/bound {ratio:.2f}"
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_varlen_backward_equal_lengths_match_batched_bitwise(D):
+    from apex_attn import (custom_attention_backward, custom_attention_forward,
+                           custom_attention_varlen_backward, custom_attention_varlen_forward)
+    B, N, H = 3, 700, 4
+    g = torch.Generator(device="cuda").manual_seed(D + 1)
+    q, k, v, do = (torch.randn(B, N, H, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(4))
+    t = lambda x: x.transpose(1, 2)
+    ob, lb = custom_attention_forward(t(q), t(k), t(v), causal=True, return_lse=True)
+    gb = custom_attention_backward(t(q), t(k), t(v), ob, lb, t(do), causal=True)
+    cu = torch.arange(0, (B + 1) * N, N, dtype=torch.int32, device="cuda")
+    p = lambda x: x.reshape(B * N, H, D)
+    ov, lv = custom_attention_varlen_forward(p(q), p(k), p(v), cu, N, causal=True, return_lse=True)
+    gv = custom_attention_varlen_backward(p(q), p(k), p(v), ov, lv, p(do), cu, N, causal=True)
+    torch.cuda.synchronize()
+    for a, b in zip(gv, gb):
+        assert torch.equal(a.reshape(B, N, H, D), b.transpose(1, 2))
+
+
+def test_varlen_backward_malformed_offsets_stay_in_bounds():
+    from apex_attn import custom_attention_varlen_backward, device_status
+    total, H, D = 500, 2, 64
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q = torch.randn(total, H, D, generator=g, device="cuda").to(torch.bfloat16)
+    lse = torch.zeros(H, total, device="cuda")
+    cu = torch.tensor([0, 300, 200, 900], dtype=torch.int32, device="cuda")
+    dq, dk, dv = custom_attention_varlen_backward(q, q, q, q, lse, q, cu, 256, causal=False)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    for t in (dq, dk, dv):
+        assert torch.isfinite(t.float()).all()

@@ -161,7 +161,8 @@ def _c_layout(struct: str, fields: list[str]) -> list[int]:
 
 @pytest.mark.parametrize("cls,struct", [(_lib.FwdArgs, "apex_attn_fwd_args"),
                                         (_lib.BwdArgs, "apex_attn_bwd_args"),
-                                        (_lib.VarlenArgs, "apex_attn_varlen_args")])
+                                        (_lib.VarlenArgs, "apex_attn_varlen_args"),
+                                        (_lib.BwdVarlenArgs, "apex_attn_bwd_varlen_args")])
 def test_ctypes_structs_match_c_compiler_layout(cls, struct):
     import shutil
     if shutil.which("gcc") is None:
@@ -242,3 +243,35 @@ def test_varlen_argument_validation(lib, kw, code):
 
 def test_varlen_null_args(lib):
     assert lib.apex_attn_fwd_varlen(None, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def _bwd_varlen_args(**kw):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, o=FAKE, dout=FAKE, lse=FAKE, dq=FAKE, dk=FAKE, dv=FAKE,
+             cu_seqlens=FAKE, batch=3, heads_q=4, heads_kv=2, total=1000, max_seqlen=500,
+             head_dim=128, dtype=0, causal=1, window_left=-1, sm_scale=0.088)
+    strides = kw.pop("strides", [512, 128, 256, 128, 256, 128, 512, 128, 512, 128, 512, 128, 256, 128, 256, 128])
+    a.update(kw)
+    return _lib.BwdVarlenArgs(strides=(ctypes.c_longlong * 16)(*strides), **a)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(cu_seqlens=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(dout=None), _lib.ERR_INVALID_ARGUMENT),
+    (dict(total=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(heads_kv=3), _lib.ERR_INVALID_ARGUMENT),
+    (dict(head_dim=256), _lib.ERR_UNSUPPORTED_HEAD_DIM),
+    (dict(sm_scale=0.0), _lib.ERR_BAD_SCALE),
+    (dict(strides=[512, 120] + [256, 128] * 7), _lib.ERR_BAD_LAYOUT),
+    (dict(cu_seqlens=FAKE + 2), _lib.ERR_BAD_LAYOUT),
+    (dict(dk=FAKE + 8), _lib.ERR_BAD_LAYOUT),
+])
+def test_bwd_varlen_argument_validation(lib, kw, code):
+    a = _bwd_varlen_args(**kw)
+    assert lib.apex_attn_bwd_varlen(ctypes.byref(a), FAKE, 1 << 24, None) == code
+
+
+def test_bwd_varlen_workspace_checks(lib):
+    a = _bwd_varlen_args()
+    need = lib.apex_attn_bwd_workspace_bytes(3, 4, 500)
+    assert lib.apex_attn_bwd_varlen(ctypes.byref(a), FAKE, need - 16, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.apex_attn_bwd_varlen(None, FAKE, need, None) == _lib.ERR_INVALID_ARGUMENT
