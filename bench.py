@@ -250,51 +250,45 @@ def bench_backward(name, c, steps, warmup, device):
             "launches_per_step": "prep + dK/dV pass + dQ pass (+ 2 counter memsets)"}
 
 
-def bench_e2e(c, steps, warmup, device):
-    """Same metric through the public API with host buffers. Every step copies its own q/k/v
-    from pinned host memory to the device, runs the forward and copies its o and lse back.
-    The steps are pipelined the way a serving or training loop overlaps I/O: uploads on one
-    stream, the operator on a second, downloads on a third, with two device buffer sets, so
-    step s+1's upload and step s-1's download run during step s's kernel and the two copy
-    directions overlap each other (PCIe is full duplex). The timed region spans the first
-    upload to the last download."""
-    from apex_attn import custom_attention_forward
-    qd, kd, vd = make_device_inputs(c, 42, device)
-    hq, hk, hv = (t.cpu().pin_memory() for t in (qd, kd, vd))
-    del qd, kd, vd
+def pipelined_e2e(host_in, op, steps, warmup, device):
+    """Runs `op` end to end over host buffers: every step copies its own inputs (`host_in`,
+    pinned) to the device, runs op(*inputs) -> outputs, and copies every output back to
+    pinned host memory. Steps are pipelined the way a serving or training loop overlaps
+    I/O: uploads on one stream, the operator on a second, downloads on a third, two device
+    buffer sets, so step s+1's upload and step s-1's download run during step s's kernel
+    and the two copy directions overlap (PCIe is full duplex). Returns (ms for `steps`
+    steps from the first upload to the last download, bytes up and down per step)."""
     n_sets = 2
-    dev_in = [tuple(torch.empty(hq.shape, dtype=hq.dtype, device=device) for _ in range(3)) for _ in range(n_sets)]
-    ho = [torch.empty(hq.shape, dtype=hq.dtype).pin_memory() for _ in range(n_sets)]
-    hl = [torch.empty(hq.shape[:3], dtype=torch.float32).pin_memory() for _ in range(n_sets)]
+    dev_in = [tuple(torch.empty(h.shape, dtype=h.dtype, device=device) for h in host_in) for _ in range(n_sets)]
+    host_out = [None] * n_sets
     up, comp, down = (torch.cuda.Stream(device) for _ in range(3))
-    done_compute = [None] * n_sets  # event: compute of the set's last step finished (inputs free)
-    done_down = [None] * n_sets     # event: download of the set's last step finished (outputs free)
+    done_compute = [None] * n_sets  # compute of the set's last step finished: inputs reusable
+    done_down = [None] * n_sets     # download of the set's last step finished
     outs = [None] * n_sets
 
     def run(n):
         for i in range(n):
             k = i % n_sets
-            q, kk, v = dev_in[k]
             with torch.cuda.stream(up):
                 if done_compute[k] is not None:
                     up.wait_event(done_compute[k])
-                q.copy_(hq, non_blocking=True)
-                kk.copy_(hk, non_blocking=True)
-                v.copy_(hv, non_blocking=True)
+                for d, h in zip(dev_in[k], host_in):
+                    d.copy_(h, non_blocking=True)
                 uploaded = torch.cuda.Event()
                 uploaded.record(up)
             with torch.cuda.stream(comp):
                 comp.wait_event(uploaded)
                 if done_down[k] is not None:
                     comp.wait_event(done_down[k])
-                o, lse = custom_attention_forward(q, kk, v, causal=True, return_lse=True)
-                outs[k] = (o, lse)
+                outs[k] = op(*dev_in[k])
                 done_compute[k] = torch.cuda.Event()
                 done_compute[k].record(comp)
             with torch.cuda.stream(down):
                 down.wait_event(done_compute[k])
-                ho[k].copy_(o, non_blocking=True)
-                hl[k].copy_(lse, non_blocking=True)
+                if host_out[k] is None:
+                    host_out[k] = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs[k]]
+                for h, o in zip(host_out[k], outs[k]):
+                    h.copy_(o, non_blocking=True)
                 done_down[k] = torch.cuda.Event()
                 done_down[k].record(down)
 
@@ -309,9 +303,20 @@ def bench_e2e(c, steps, warmup, device):
             down.wait_event(done_down[k])
     t1.record(down)
     torch.cuda.synchronize(device)
-    total_ms = t0.elapsed_time(t1)
-    bi = 3 * hq.numel() * hq.element_size()
-    bo = ho[0].numel() * ho[0].element_size() + hl[0].numel() * 4
+    bytes_up = sum(h.numel() * h.element_size() for h in host_in)
+    bytes_down = sum(h.numel() * h.element_size() for h in host_out[0])
+    return t0.elapsed_time(t1), bytes_up, bytes_down
+
+
+def bench_e2e(c, steps, warmup, device):
+    """Same metric through the public API with host buffers (see pipelined_e2e): each step
+    uploads q/k/v, runs custom_attention_forward (with lse) and downloads o and lse."""
+    from apex_attn import custom_attention_forward
+    qd, kd, vd = make_device_inputs(c, 42, device)
+    host = tuple(t.cpu().pin_memory() for t in (qd, kd, vd))
+    del qd, kd, vd
+    op = lambda q, k, v: custom_attention_forward(q, k, v, causal=True, return_lse=True)
+    total_ms, bi, bo = pipelined_e2e(host, op, steps, warmup, device)
     return {"value": flops(c) * steps / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
             "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": total_ms / steps,
             "pipeline": "uploads, operator and downloads on three streams, two device buffer sets"}
@@ -393,30 +398,17 @@ def run_multi(args, c, rank, world, local_rank):
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         tmax = ms.item()
 
-        # End to end through the public operator: each rank copies its q/k/v shard from
-        # pinned host memory, runs the forward and copies o back, every step.
-        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-        ho = torch.empty(hq.shape, dtype=hq.dtype).pin_memory()
-
-        def e2e_step():
-            qd, kd, vd = (t.to(device, non_blocking=True) for t in (hq, hk, hv))
-            ho.copy_(custom_attention_forward(qd, kd, vd, causal=True), non_blocking=True)
-
+        # End to end through the public operator: each rank uploads its q/k/v shard from
+        # pinned host memory, runs the forward and downloads o, every step (pipelined as
+        # in bench_e2e).
+        host = tuple(t.cpu().pin_memory() for t in (q, k, v))
         e2e_steps = max(2, min(args.steps, 5))
-        for _ in range(2):
-            e2e_step()
-        torch.cuda.synchronize()
         dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ems = torch.tensor([e0.elapsed_time(e1)], device=device)
+        e_ms, _, _ = pipelined_e2e(host, lambda a, b, c_: (custom_attention_forward(a, b, c_, causal=True),),
+                                   e2e_steps, 2, device)
+        ems = torch.tensor([e_ms], device=device)
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        del hq, hk, hv, ho
+        del host
 
         o = fn()
         status = device_status(local_rank)
