@@ -227,3 +227,61 @@ def test_bwd_rejects_head_dim_256():
     lse = torch.zeros(1, 1, 128, device="cuda")
     with pytest.raises(KeyError):
         custom_attention_backward(q, q, q, q, lse, q)
+
+
+def test_bwd_concurrent_streams_match_serial_bitwise():
+    """Backward calls on three streams at once: each pass schedules with its own work-counter
+    slot and each call has its own workspace, so results equal the serial ones bit for bit."""
+    from apex_attn import custom_attention_backward, custom_attention_forward
+    cfgs = [(2, 4, 2, 1536, 64, 1), (1, 8, 8, 2048, 128, 2), (1, 6, 3, 3000, 128, 3)]
+    ins = []
+    for B, H, HKV, N, D, s in cfgs:
+        q, k, v, do = (t.cuda() for t in inputs(B, H, HKV, N, D, seed=s))
+        o, lse = custom_attention_forward(q, k, v, return_lse=True)
+        ins.append((q, k, v, o, lse, do))
+    serial = [custom_attention_backward(*x) for x in ins]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream() for _ in ins]
+    outs = []
+    for st, x in zip(streams, ins):
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            outs.append(custom_attention_backward(*x))
+    torch.cuda.synchronize()
+    for a, b in zip(serial, outs):
+        for x, y in zip(a, b):
+            assert torch.equal(x, y)
+
+
+def test_training_step_cuda_graph_capture_and_replay():
+    """Forward + backward (the attention part of a training step) captured into one CUDA
+    graph after an eager call; replays on new inputs equal eager results."""
+    from apex_attn import custom_attention_backward, custom_attention_forward
+    q, k, v, do = (t.cuda() for t in inputs(2, 4, 2, 1024, 128, seed=21))
+
+    def step():
+        o, lse = custom_attention_forward(q, k, v, return_lse=True)
+        return (o,) + tuple(custom_attention_backward(q, k, v, o, lse, do))
+
+    eager = step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()  # warm the caching allocator on this stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            outs = step()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(outs, eager):
+        assert torch.equal(a, b)
+    new = [t.cuda() for t in inputs(2, 4, 2, 1024, 128, seed=22)]
+    for dst, src in zip((q, k, v, do), new):
+        dst.copy_(src)
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(outs, step()):
+        assert torch.equal(a, b)

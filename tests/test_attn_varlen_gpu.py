@@ -194,3 +194,31 @@ def test_varlen_backward_malformed_offsets_stay_in_bounds():
     assert device_status() == 0
     for t in (dq, dk, dv):
         assert torch.isfinite(t.float()).all()
+
+
+def test_varlen_cuda_graph_capture_and_replay():
+    from apex_attn import custom_attention_varlen_backward, custom_attention_varlen_forward
+    q, k, v, cu = packed_inputs([300, 1, 700], 2, 1, 64, seed=4)
+    q, k, v = q.cuda(), k.cuda(), v.cuda()
+    do = torch.randn(q.shape, device="cuda").to(q.dtype)
+    cu = torch.from_numpy(cu).cuda()
+
+    def step():
+        o, lse = custom_attention_varlen_forward(q, k, v, cu, 700, return_lse=True)
+        return (o,) + tuple(custom_attention_varlen_backward(q, k, v, o, lse, do, cu, 700))
+
+    eager = step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            outs = step()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(outs, eager):
+        assert torch.equal(a, b)
