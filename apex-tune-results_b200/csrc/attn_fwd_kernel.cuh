@@ -77,15 +77,24 @@ struct AttnParams {
 };
 
 // Per-head-dim configuration (replaces _CONFIGS, fused_attention.py:148-152).
+#ifndef APEX_FWD_CS64
+#define APEX_FWD_CS64 2
+#endif
+
 template <int D>
 struct Cfg {
   static_assert(D == 64 || D == 128 || D == 256, "head dims 64, 128, 256");
   static constexpr int kSub = D == 256 ? 1 : 2;          // 128-row query sub-tiles per item
+  // Softmax warpgroups per sub-tile: each takes kBlockN / kCS of the tile's key columns for
+  // all 128 rows (row max exchanged through shared memory, row sums added in the
+  // epilogue). Two per sub-tile put four softmax warps on every SM sub-partition, so
+  // one warp's loads, row max and P store overlap another's exponentials.
+  static constexpr int kCS = D == 64 ? APEX_FWD_CS64 : 1;
   static constexpr bool kPInTmem = D != 128;             // else P lives in shared memory
   static constexpr int kParts = D == 256 ? 2 : 1;        // ring stages per K or V tile
   static constexpr int kStageCols = D / kParts;          // head-dim columns per stage
   static constexpr int kNS = D == 64 ? 8 : (D == 128 ? 3 : 5);  // ring stages
-  static constexpr int kThreads = 128 * (kSub + 2);
+  static constexpr int kThreads = 128 * (kSub * kCS + 2);
   static constexpr int kItemRows = kSub * kBlockM;
   // TMEM columns: S_i at i*128; O_i at kTmemO + i*D; P_i at kTmemP + i*64 (TMEM variants).
   static constexpr int kTmemO = 256;
@@ -93,12 +102,13 @@ struct Cfg {
   // setmaxnreg budgets (multiples of 8): softmax, epilogue, the remaining warpgroup. Their
   // sum x 128 must not exceed the launch allocation (kThreads x (65536 / kThreads)), or
   // setmaxnreg.inc would wait forever; checked below.
-  static constexpr int kRegsSoftmax = kSub == 2 ? 184 : 240;
-  static constexpr int kRegsEpilogue = kSub == 2 ? 80 : 128;
-  static constexpr int kRegsOther = kSub == 2 ? 56 : 136;
+  static constexpr int kRegsSoftmax = kCS == 2 ? 88 : (kSub == 2 ? 184 : 240);
+  static constexpr int kRegsEpilogue = kCS == 2 ? 64 : (kSub == 2 ? 80 : 128);
+  static constexpr int kRegsOther = kCS == 2 ? 48 : (kSub == 2 ? 56 : 136);
   static constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
-  static_assert(128 * (kSub * kRegsSoftmax + kRegsEpilogue + kRegsOther) <= kThreads * kLaunchRegs,
+  static_assert(128 * (kSub * kCS * kRegsSoftmax + kRegsEpilogue + kRegsOther) <= kThreads * kLaunchRegs,
                 "setmaxnreg split exceeds the launch register allocation");
+  static_assert(kCS == 1 || kPInTmem, "split softmax columns need P in TMEM");
   static_assert(kTmemO + kSub * D <= 512, "TMEM plan overflows 512 columns");
   static_assert(!kPInTmem || kTmemP + kSub * 64 <= kTmemO || kTmemP >= kTmemO + kSub * D,
                 "P columns overlap O");
@@ -175,11 +185,15 @@ struct SmemPlan {
   static constexpr int kLFull = kOEmpty + S;
   static constexpr int kLEmpty = kLFull + S;
   static constexpr int kDrain = kLEmpty + S;
-  static constexpr int kItemFull = kDrain + S;          // [kItemRing]
+  static constexpr int kMaxX = kDrain + S;              // [S * kCS] row-max exchange (kCS = 2)
+  static constexpr int kItemFull = kMaxX + S * C::kCS;  // [kItemRing]
   static constexpr int kItemEmpty = kItemFull + kItemRing;  // [kItemRing]
   static constexpr int kNumBars = kItemEmpty + kItemRing;
-  static constexpr int kRowStats = (kBars + kNumBars * 8 + 15) / 16 * 16;  // float l[S][128], m[S][128]
-  static constexpr int kItems = kRowStats + 2 * S * kBlockM * 4;           // int item[kItemRing]
+  // float l[S * kCS][128] (partial row sums), m[S][128]; then (kCS = 2) the row-max
+  // exchange float x[S][kCS][2 tiles][128].
+  static constexpr int kRowStats = (kBars + kNumBars * 8 + 15) / 16 * 16;
+  static constexpr int kXch = kRowStats + (C::kCS + 1) * S * kBlockM * 4;
+  static constexpr int kItems = kXch + (C::kCS == 2 ? S * 2 * 2 * kBlockM * 4 : 0);  // int item[kItemRing]
   static constexpr int kMisc = kItems + kItemRing * 4;                      // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kMaxDynamic = 232448;  // 227 KB per CTA on sm_100
@@ -402,13 +416,14 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
 
   const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0);
   const int lane = (int)(threadIdx.x & 31);
-  constexpr int kWarpEpi = 4 * SUB;       // first epilogue warp
+  constexpr int CS = C::kCS;
+  constexpr int kWarpEpi = 4 * SUB * CS;  // first epilogue warp
   constexpr int kWarpMma = kWarpEpi + 4;  // first MMA warp
   constexpr int kWarpProd = kWarpMma + SUB;
 
   auto bar = [&](int slot) -> uint32_t { return sbase + Plan::kBars + slot * 8; };
-  float* row_l = reinterpret_cast<float*>(smem + Plan::kRowStats);   // [SUB][128]
-  float* row_m = row_l + SUB * kBlockM;                               // [SUB][128]
+  float* row_l = reinterpret_cast<float*>(smem + Plan::kRowStats);   // [SUB * CS][128]
+  float* row_m = row_l + SUB * CS * kBlockM;                          // [SUB][128]
   int* items = reinterpret_cast<int*>(smem + Plan::kItems);           // [kItemRing]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Plan::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Plan::kMisc + 4);
@@ -422,18 +437,19 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       ptx::mbar_init(bar(Plan::kQFull + i), 1);
       ptx::mbar_init(bar(Plan::kQEmpty + i), 1);
       ptx::mbar_init(bar(Plan::kSFull + i), 1);
-      ptx::mbar_init(bar(Plan::kSFree + i), kBlockM);
-      ptx::mbar_init(bar(Plan::kPFull + i), kBlockM);
+      ptx::mbar_init(bar(Plan::kSFree + i), kBlockM * CS);
+      ptx::mbar_init(bar(Plan::kPFull + i), kBlockM * CS);
       ptx::mbar_init(bar(Plan::kPFree + i), 1);
       ptx::mbar_init(bar(Plan::kOFull + i), 1);
       ptx::mbar_init(bar(Plan::kOEmpty + i), kBlockM);
-      ptx::mbar_init(bar(Plan::kLFull + i), kBlockM);
+      ptx::mbar_init(bar(Plan::kLFull + i), kBlockM * CS);
       ptx::mbar_init(bar(Plan::kLEmpty + i), kBlockM);
       ptx::mbar_init(bar(Plan::kDrain + i), 1);
+      for (int h = 0; h < CS; ++h) ptx::mbar_init(bar(Plan::kMaxX + i * CS + h), kBlockM);
     }
     // Readers of the item ring: softmax, epilogue and MMA warps, and the Q producer of
     // sub-tile 1 (the ring producer writes it).
-    constexpr int kItemReaders = 4 * SUB + 4 + SUB + (SUB - 1);
+    constexpr int kItemReaders = 4 * SUB * CS + 4 + SUB + (SUB - 1);
     for (int k = 0; k < kItemRing; ++k) {
       ptx::mbar_init(bar(Plan::kItemFull + k), 1);
       ptx::mbar_init(bar(Plan::kItemEmpty + k), kItemReaders);
@@ -459,13 +475,18 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
   if (warp < kWarpEpi) {
     // =========================================================== softmax ===
     ptx::setmaxnreg_inc<C::kRegsSoftmax>();
-    const int i = warp >> 2;            // sub-tile
+    constexpr int kCols = kBlockN / CS;  // key columns of the tile this warpgroup handles
+    constexpr int NH = kCols / 64;       // 64-key halves among them
+    const int i = (warp >> 2) / CS;     // sub-tile
+    const int cs = (warp >> 2) % CS;    // column part: keys [cs * kCols, (cs + 1) * kCols)
     const int quarter = warp & 3;       // TMEM lane quarter
     const int r = quarter * 32 + lane;  // row within the sub-tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128);
+    const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128 + cs * kCols);
     const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
-    const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64);
+    const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64 + cs * (kCols / 2));
+    float* xch = reinterpret_cast<float*>(smem + Plan::kXch);  // [SUB][CS][2][128]
+    int tcount = 0;  // tiles this warpgroup processed (row-max exchange slot and parity)
     // Row r of P in shared memory: two 16 KB chunks (keys 0-63, 64-127) of the SW128
     // K-major layout; 16-byte unit u of the row sits at unit position u ^ (r & 7).
     const uint32_t sP = sbase + Plan::kP + i * Plan::kPTileBytes + r * 128;
@@ -489,14 +510,14 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         if (!(ok = W.wait_warp(bar(Plan::kSFull + i), s_par))) break;
         s_par ^= 1;
         ptx::tc_fence_after();
-        float s[kBlockN];
+        float s[kCols];
         {
-          uint32_t v[kBlockN / 32][32];
+          uint32_t v[kCols / 32][32];
 #pragma unroll
-          for (int ch = 0; ch < kBlockN / 32; ++ch) ptx::tmem_ld32(tS + ch * 32, v[ch]);
+          for (int ch = 0; ch < kCols / 32; ++ch) ptx::tmem_ld32(tS + ch * 32, v[ch]);
           ptx::tmem_wait_ld();
 #pragma unroll
-          for (int ch = 0; ch < kBlockN / 32; ++ch) {
+          for (int ch = 0; ch < kCols / 32; ++ch) {
             ptx::reg_fence32(v[ch]);  // no use of the loaded values above the wait
 #pragma unroll
             for (int e = 0; e < 32; ++e) s[ch * 32 + e] = __uint_as_float(v[ch][e]);
@@ -516,20 +537,31 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
           const int kv_limit = diag_tile ? r + 1 : (tail_tile ? kv_last_valid : kBlockN);  // keys >= limit masked
           const int kv_first = win_tile ? r0 + r - p.window - j * kBlockN : 0;            // keys < first masked
 #pragma unroll
-          for (int e = 0; e < kBlockN; ++e)
-            if (e >= kv_limit || e < kv_first) s[e] = -INFINITY;
+          for (int e = 0; e < kCols; ++e)
+            if (e + cs * kCols >= kv_limit || e + cs * kCols < kv_first) s[e] = -INFINITY;
         }
         float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
         float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
         static_assert(kBlockN % 8 == 0, "row max consumes 8 scores per step");
 #pragma unroll
-        for (int e = 8; e < kBlockN; e += 8) {
+        for (int e = 8; e < kCols; e += 8) {
           mx0 = ptx::fmax3(mx0, s[e], s[e + 1]);
           mx1 = ptx::fmax3(mx1, s[e + 2], s[e + 3]);
           mx2 = ptx::fmax3(mx2, s[e + 4], s[e + 5]);
           mx3 = ptx::fmax3(mx3, s[e + 6], s[e + 7]);
         }
-        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;  // log2 domain
+        float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;  // log2 domain
+        if (CS == 2) {
+          // Row max over the whole tile: publish this part's max, take the partner's. Slots
+          // alternate by tile; a slot is rewritten two tiles later, after the partner has
+          // read it (it reads tile t before it can reach the exchange of tile t + 1).
+          const int slot = tcount & 1;
+          xch[((i * CS + cs) * 2 + slot) * kBlockM + r] = mx;
+          ptx::mbar_arrive(bar(Plan::kMaxX + i * CS + cs));
+          if (!(ok = W.wait_warp(bar(Plan::kMaxX + i * CS + (1 - cs)), (uint32_t)slot))) break;
+          mx = fmaxf(mx, xch[((i * CS + (1 - cs)) * 2 + slot) * kBlockM + r]);
+        }
+        ++tcount;
         float alpha = 1.f;
         bool resc = false;
         if (j == lo) {
@@ -544,7 +576,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         const float m_use = (WIN && m == -INFINITY) ? 0.f : m;  // all keys masked: p = 0, not NaN
         const float2 nm2 = make_float2(-m_use, -m_use);
         float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
-        uint32_t pk[2][32];
+        uint32_t pk[NH][32];
         auto exp_half = [&](const int half, auto poly) {
           constexpr bool kPoly = decltype(poly)::value;
 #pragma unroll
@@ -558,12 +590,10 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
             pk[half][e] = DType<T>::pack(pr.x, pr.y);
           }
         };
-        if (masked) {  // masked keys hold -inf: MUFU gives exactly 0 for them
-          exp_half(0, std::false_type{});
-          exp_half(1, std::false_type{});
-        } else {
-          exp_half(0, std::integral_constant<bool, (EMU8 > 0)>{});
-          exp_half(1, std::integral_constant<bool, (EMU8 > 0)>{});
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          if (masked) exp_half(h, std::false_type{});  // masked keys hold -inf: MUFU gives exactly 0
+          else exp_half(h, std::integral_constant<bool, (EMU8 > 0)>{});
         }
         const float2 sum = __fadd2_rn(sa, sb);
         l += sum.x + sum.y;
@@ -577,7 +607,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         if (__any_sync(0xffffffffu, resc)) {
           // O is quiescent: the previous P.V completed (above) and the next waits for P.
 #pragma unroll 1
-          for (int ch = 0; ch < D / 32; ++ch) {
+          for (int ch = cs * (D / 32 / CS); ch < (cs + 1) * (D / 32 / CS); ++ch) {  // this part's O columns
             uint32_t v[32];
             ptx::tmem_ld32(tO + ch * 32, v);
             ptx::tmem_wait_ld();
@@ -588,12 +618,12 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
           }
         }
         if (C::kPInTmem) {
-          ptx::tmem_st32(tP, pk[0]);
-          ptx::tmem_st32(tP + 32, pk[1]);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) ptx::tmem_st32(tP + h * 32, pk[h]);
           ptx::tmem_wait_st();
         } else {
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < NH; ++h)
 #pragma unroll
             for (int u = 0; u < 8; ++u)
               ptx::st_shared_v4(sP + h * Plan::kChunkBytes + ((u ^ (r & 7)) << 4), pk[h][4 * u],
@@ -607,8 +637,8 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       if (!ok) break;
       if (!(ok = W.wait_warp(bar(Plan::kLEmpty + i), le_par))) break;
       le_par ^= 1;
-      row_l[i * kBlockM + r] = l;
-      row_m[i * kBlockM + r] = m;
+      row_l[(i * CS + cs) * kBlockM + r] = l;  // this part's share of the row sum
+      if (cs == 0) row_m[i * kBlockM + r] = m;
       ptx::mbar_arrive(bar(Plan::kLFull + i));
     }
   } else if (warp < kWarpMma) {
@@ -621,7 +651,8 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     auto finish = [&](const WorkItem& it, const int i) -> bool {
       if (!W.wait_warp(bar(Plan::kLFull + i), (lf_par >> i) & 1u)) return false;
       lf_par ^= 1u << i;
-      const float l = row_l[i * kBlockM + r];
+      float l = row_l[(i * CS) * kBlockM + r];
+      if (CS == 2) l += row_l[(i * CS + 1) * kBlockM + r];
       const float m = row_m[i * kBlockM + r];
       ptx::mbar_arrive(bar(Plan::kLEmpty + i));
       if (!W.wait_warp(bar(Plan::kOFull + i), (of_par >> i) & 1u)) return false;
