@@ -786,6 +786,19 @@ int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, 
                  sm_scale, strides, stream);
 }
 
+int apex_attn_num_sms_hint(int device) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_NO_DEVICE;
+  }
+  if (device < 0 || device >= count || device >= kMaxDevices) return APEX_ATTN_ERR_NO_DEVICE;
+  DeviceState probe;
+  std::lock_guard<std::mutex> lk(g_mu);
+  const int rc = probe_device_locked(device, probe);
+  return rc == APEX_ATTN_OK ? probe.num_sms : rc;
+}
+
 int apex_attn_device_status(int device, int* flags) {
   if (!flags) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(device);

@@ -263,6 +263,12 @@ typedef struct apex_attn_bwd_varlen_args {
 int apex_attn_bwd_varlen(const apex_attn_bwd_varlen_args* args, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* Number of SMs of `device` (the persistent kernels' grid is min(work items, this)), or a
+ * negative status: APEX_ATTN_ERR_NO_DEVICE for a bad ordinal or no device,
+ * APEX_ATTN_ERR_UNSUPPORTED_ARCH if it is not sm_100. Lets a caller size its own batching
+ * (e.g. how many heads make a full wave). No counterpart in the reference. */
+int apex_attn_num_sms_hint(int device);
+
 /* Human-readable text for a status code. Replaces the exception text the reference
  * harness prints on failure (submission.py:299-306). */
 const char* apex_attn_strerror(int status);

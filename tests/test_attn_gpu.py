@@ -291,3 +291,10 @@ def test_cuda_graph_capture_and_replay():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, custom_attention_forward(q2, k2, v2))
+
+
+def test_num_sms_hint_is_the_device_sm_count():
+    from apex_attn import _lib
+    lib = _lib.load()
+    assert lib.apex_attn_num_sms_hint(0) == torch.cuda.get_device_properties(0).multi_processor_count
+    assert lib.apex_attn_num_sms_hint(torch.cuda.device_count()) == _lib.ERR_NO_DEVICE

@@ -275,3 +275,11 @@ def test_bwd_varlen_workspace_checks(lib):
     need = lib.apex_attn_bwd_workspace_bytes(3, 4, 500)
     assert lib.apex_attn_bwd_varlen(ctypes.byref(a), FAKE, need - 16, None) == _lib.ERR_INVALID_ARGUMENT
     assert lib.apex_attn_bwd_varlen(None, FAKE, need, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_num_sms_hint_without_device(lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("checks the no-device path")
+    assert lib.apex_attn_num_sms_hint(0) == _lib.ERR_NO_DEVICE
+    assert lib.apex_attn_num_sms_hint(-1) == _lib.ERR_NO_DEVICE
