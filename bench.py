@@ -58,9 +58,9 @@ MLS_SHAPES = {64: dict(B=4, H=32, N=4096, D=64), 128: dict(B=2, H=16, N=8192, D=
 PUBLISHED_H100_TFLOPS = {64: 430.7, 128: 468.4, 256: 451.7}
 
 # DRAM traffic of one C3 launch (dram__bytes_read.sum + dram__bytes_write.sum) from an ncu
-# capture of this kernel: 1.677 GB read + 0.260 GB write. Algorithmic bytes of C3: q, k, v
+# capture of this kernel: 0.874 GB read + 0.254 GB write. Algorithmic bytes of C3: q, k, v
 # read (3 x 268 MB) + o written (268 MB) + fp32 lse (4.2 MB).
-TRAFFIC_C3_BYTES = 1.677466e9 + 0.260146e9
+TRAFFIC_C3_BYTES = 0.874267392e9 + 0.254193920e9
 ALGO_BYTES_C3 = 4 * 4 * 32 * 8192 * 128 * 2 + 4 * 32 * 8192 * 4
 
 
