@@ -31,9 +31,12 @@ using apex::AttnParams;
 constexpr int kVersion = 300;  // 0.3.0
 
 // Build-time tuning knob (overridable with -D for sweeps): exp2 pairs out of every 8 of an
-// unmasked tile that use the FMA-pipe polynomial, per head dim.
+// unmasked tile that use the FMA-pipe polynomial, per head dim. At d = 64 four softmax warps
+// share each sub-partition and leave issue slots free beside MUFU: one pair in eight on the
+// FMA pipe measured +4-5 % (C2 573-580 -> 601-604 TFLOP/s, fp16 MLS d64 651 -> 680); two
+// in eight the same, three in eight slower. d = 128 and 256 measured no gain.
 #ifndef APEX_EMU64
-#define APEX_EMU64 0
+#define APEX_EMU64 1
 #endif
 #ifndef APEX_EMU128
 #define APEX_EMU128 0
