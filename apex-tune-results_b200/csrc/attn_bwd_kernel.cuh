@@ -55,11 +55,16 @@
 #define APEX_BWD_SPLIT_DP_KV 1
 #endif
 // Of every 8 pairs of exponentials in an unmasked tile, how many the elementwise warps take
-// from the FMA-pipe polynomial (exp2_poly_pair) instead of MUFU ex2. Both warpgroups run
-// their exponentials at the same time, which is MUFU-bound (16 per clock per SM) while
-// the FMA pipe idles.
-#ifndef APEX_BWD_EMU
-#define APEX_BWD_EMU 0
+// from the FMA-pipe polynomial (exp2_poly_pair) instead of MUFU ex2, per head dim. Both
+// warpgroups run their exponentials at the same time, which is MUFU-bound (16 per clock per
+// SM) while the FMA pipe idles. Measured with both builds alternating call by call in one
+// process: at d = 64 two pairs in eight take the C2 backward from 0.627 to 0.603 ms (one
+// pair: 0.621); at d = 128 one or two pairs are within run-to-run noise (6.74-6.82 ms).
+#ifndef APEX_BWD_EMU64
+#define APEX_BWD_EMU64 2
+#endif
+#ifndef APEX_BWD_EMU128
+#define APEX_BWD_EMU128 0
 #endif
 
 namespace apex {
@@ -289,7 +294,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
   using C = BwdCfg<D>;
   using Plan = BwdSmem<D>;
   constexpr int NS = C::kNS;
-  constexpr int kEmu = APEX_BWD_EMU;
+  constexpr int kEmu = D == 64 ? APEX_BWD_EMU64 : APEX_BWD_EMU128;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   if (Plan::kDynamicBytes == Plan::kBytes && (raw_addr & 1023u) != 0) {
