@@ -366,7 +366,36 @@ int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUt
   const double kv_bytes_per_head = 2.0 * p.N * head_dim * 2.0 / p.kv_group;
   long long g = (long long)(48.0 * 1024 * 1024 / kv_bytes_per_head);
   g = std::max(1LL, std::min(g, BH));
-  const long long ngroups = (BH + g - 1) / g;
+  long long ngroups = (BH + g - 1) / g;
+  // Load balance across the groups: items run longest first inside a group, but the groups
+  // run one after another, so the last group's longest item starts when about
+  // (1 - 1/ngroups) of the work is done and must fit in the work left. Allow at most
+  // (work per SM) / (1.25 x longest item) groups; item work counts the K/V tiles of its
+  // busiest sub-tile. Shapes with many items per SM are not limited (the bound is only
+  // evaluated up to 4096 query blocks). Measured against the L2 bound alone: the MLS
+  // shapes d=128 (32 heads, N=8192) 3 -> 2 groups +2-3 % and d=256 (8 heads, N=16384)
+  // 3 -> 2 groups +8-9 %; C3 keeps its 11 groups (a factor of 1.5 would give 9, -0.5 %).
+  if (ngroups > 1 && mblocks <= 4096) {
+    const int sub_rows = apex::kBlockM;
+    const int ksub = rows_per_item / sub_rows;
+    double sum_tiles = 0.0;
+    long long max_tiles = 1;
+    for (long long mb = 0; mb < mblocks; ++mb) {
+      long long tiles = 0;
+      for (int i = 0; i < ksub; ++i) {
+        const long long r0 = mb * rows_per_item + (long long)i * sub_rows;
+        if (r0 >= p.N) break;
+        const long long nb = p.causal ? std::min<long long>(p.num_kblocks, r0 / apex::kBlockN + 1) : p.num_kblocks;
+        const long long lo = p.window >= 0 ? std::max<long long>(0, r0 - p.window) / apex::kBlockN : 0;
+        tiles = std::max(tiles, nb - lo);
+      }
+      sum_tiles += (double)tiles;
+      max_tiles = std::max(max_tiles, tiles);
+    }
+    const double work_per_sm = (double)BH * sum_tiles / std::max(1, ds->num_sms);
+    const long long balance = std::max(1LL, (long long)(work_per_sm / (1.25 * (double)max_tiles)));
+    ngroups = std::min(ngroups, balance);
+  }
   p.group_q = (int)(BH / ngroups);
   p.group_big = (int)(BH % ngroups);
   p.work_counter = ds->status + kCounterBase + (int)(g_counter_seq.fetch_add(1) % kCounterSlots);
