@@ -141,8 +141,9 @@ int init_device(int dev, DeviceState** out) {
 // inference server owns the whole device budget, a plugin loaded into a host that
 // forbids allocations outside its own allocator, or a real-time loop in which an
 // allocation (and the device synchronisation it may imply) is not allowed. For them the
-// forward kernel's only scratch memory, the device status word that its bounded waits
-// write on a timeout, lives in the fixed array below instead of a cudaMalloc'd buffer.
+// forward kernel's scratch memory (the device status word that its bounded waits write on
+// a timeout, and the scheduler's work-item counter) lives in the fixed array below
+// instead of a cudaMalloc'd buffer.
 //
 // Every device that loads this library holds this array (256 bytes) until the process
 // exits. A launch uses 8 bytes of it (the status word and one work-item counter, in the

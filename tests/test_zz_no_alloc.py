@@ -3,9 +3,9 @@
 Some callers of this library cannot call cudaMalloc: for example a serving runtime or
 memory pool that owns the device budget, or a plugin whose host forbids allocations
 outside its own allocator. apex_attn_fwd_noalloc serves them by keeping the kernel's
-scratch (the device status word) in a fixed static device array instead of a
-cudaMalloc'd buffer. The caller (here: the test, through torch) still allocates the
-inputs and outputs.
+scratch (the device status word and the scheduler's work-item counter) in a fixed static
+device array instead of a cudaMalloc'd buffer. The caller (here: the test, through torch)
+still allocates the inputs and outputs.
 
 This file is named so that pytest collects it last: if it fails, a run that stops at
 the first failure has already run every other test. It must pass both alone in a fresh
