@@ -99,7 +99,9 @@ SYMBOLS = {
     "apex_attn_bwd_varlen": (ctypes.c_int, [ctypes.POINTER(BwdVarlenArgs), ctypes.c_void_p,
                                             ctypes.c_size_t, ctypes.c_void_p]),
     "apex_attn_num_sms_hint": (ctypes.c_int, [ctypes.c_int]),
+    "apex_attn_set_forward_kernel": (ctypes.c_int, [ctypes.c_int]),
     "apex_attn_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "apex_attn_noalloc_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "apex_attn_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p]),
     "apex_attn_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "apex_attn_version": (ctypes.c_int, []),

@@ -18,6 +18,10 @@ What it does, as the harness does:
   submission.py:243-261);
 * reports TFLOP/s with 4*B*N^2*H*d FLOPs, halved for causal (submission.py:235-240), and
   ``speedup_vs_sdpa``.
+
+Its command line, its metric lines and its timing loop restate submission.py:243-341 on
+purpose: they are the protocol the runner's parser reads, so they must match it. The
+kernel it drives is this package's own.
 """
 from __future__ import annotations
 

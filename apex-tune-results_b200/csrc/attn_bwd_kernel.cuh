@@ -77,6 +77,7 @@ struct BwdParams {
   const float* nlse2;    // workspace [B * H][Npad]: -lse * log2(e), -inf on padding rows
   const float* ndelta;   // workspace [B * H][Npad]: -rowsum(dO * O), 0 on padding rows
   int* status;
+  int* host_flag;  // nullable: mapped pinned host word set to 1 with any status bit
   int* work_counter;
   int B, H, Hkv, N, Npad;
   int nblk;              // ceil(N / 128)
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   if (Plan::kDynamicBytes == Plan::kBytes && (raw_addr & 1023u) != 0) {
     // The plan needs the whole 227 KB and the base is not 1 KB aligned: report, do nothing.
-    if (threadIdx.x == 0) atomicOr(p.status, kStatusSmemAlign);
+    if (threadIdx.x == 0) report_error(p.status, p.host_flag, kStatusSmemAlign);
     return;
   }
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const Waiter W{abort_flag, p.status, p.timeout_ns};
+  const Waiter W{abort_flag, p.status, p.timeout_ns, p.host_flag};
 
   if (warp < C::kWarpMma) {
     // ======================================================== elementwise ===
@@ -741,7 +742,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     }
     if (ok && pend.valid) ok = accumulate(pend);
     ptx::tc_commit_warp(bar(Plan::kDrain));
-    if (lane == 0) drain_wait(bar(Plan::kDrain), 0, p.timeout_ns, p.status);
+    if (lane == 0) drain_wait(bar(Plan::kDrain), 0, p.timeout_ns, p.status, p.host_flag);
     __syncwarp();
   } else {
     ptx::setmaxnreg_dec<C::kRegsOther>();
@@ -814,11 +815,11 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       const int last = fills < NS ? fills : NS;
       for (int k = 0; k < last; ++k) {
         const int f = fills - 1 - k;
-        drain_wait(bar(Plan::kRingFull + (f % NS)), (uint32_t)((f / NS) & 1), p.timeout_ns, p.status);
+        drain_wait(bar(Plan::kRingFull + (f % NS)), (uint32_t)((f / NS) & 1), p.timeout_ns, p.status, p.host_flag);
       }
-      if (x_fills > 0) drain_wait(bar(Plan::kXFull), (uint32_t)((x_fills - 1) & 1), p.timeout_ns, p.status);
+      if (x_fills > 0) drain_wait(bar(Plan::kXFull), (uint32_t)((x_fills - 1) & 1), p.timeout_ns, p.status, p.host_flag);
       for (int k = stat_fills > 2 ? stat_fills - 2 : 0; k < stat_fills; ++k)
-        drain_wait(bar(Plan::kStatsFull + (k & 1)), (uint32_t)(k >> 1) & 1u, p.timeout_ns, p.status);
+        drain_wait(bar(Plan::kStatsFull + (k & 1)), (uint32_t)(k >> 1) & 1u, p.timeout_ns, p.status, p.host_flag);
     }
     __syncwarp();
   }

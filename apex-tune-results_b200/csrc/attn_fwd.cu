@@ -23,6 +23,7 @@
 #include "apex_attn.h"
 #include "attn_bwd_kernel.cuh"
 #include "attn_fwd_kernel.cuh"
+#include "attn_fwd_tile_kernel.cuh"
 
 namespace {
 
@@ -48,6 +49,19 @@ constexpr int kVersion = 300;  // 0.3.0
 #endif
 template <int D>
 constexpr int kEmu = D == 64 ? APEX_EMU64 : (D == 128 ? APEX_EMU128 : APEX_EMU256);
+// The same knob for the tile kernel (attn_fwd_tile_kernel), per head dim.
+#ifndef APEX_TILE_EMU64
+#define APEX_TILE_EMU64 1
+#endif
+#ifndef APEX_TILE_EMU128
+#define APEX_TILE_EMU128 2
+#endif
+template <int D>
+constexpr int kEmuTile = D == 64 ? APEX_TILE_EMU64 : APEX_TILE_EMU128;
+
+// Forward kernel selection (apex_attn_set_forward_kernel): 0 = automatic, 1 = the
+// two-sub-tile kernel for every call, 2 = the tile kernel wherever it applies.
+std::atomic<int> g_fwd_kind{0};
 
 constexpr int kMaxDevices = 64;
 // Per-device scratch of the kernel: int[64]. Word 0 is the status word; words
@@ -63,9 +77,14 @@ std::atomic<unsigned> g_counter_seq{0};
 struct DeviceState {
   bool ready = false;
   int* status = nullptr;
+  // Mapped pinned host word that kernels set to 1 when they record a device-side error
+  // (host address, and the address kernels use); null on the allocation-free path.
+  int* host_flag = nullptr;
+  int* host_flag_dev = nullptr;
   int num_sms = 0;
   int cc_major = 0, cc_minor = 0;
   unsigned attr_done = 0;  // bit per kernel instantiation
+  unsigned attr_tile = 0;  // bit per tile-kernel instantiation
   unsigned attr_bwd = 0;   // bit per backward kernel instantiation
 };
 
@@ -128,9 +147,30 @@ int init_device(int dev, DeviceState** out) {
       (void)cudaGetLastError();
       return APEX_ATTN_ERR_CUDA;
     }
+    void* hf = nullptr;
+    void* hf_dev = nullptr;
+    if (cudaHostAlloc(&hf, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
+        cudaHostGetDevicePointer(&hf_dev, hf, 0) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_CUDA;
+    }
+    *static_cast<volatile int*>(hf) = 0;
+    s.host_flag = static_cast<int*>(hf);
+    s.host_flag_dev = static_cast<int*>(hf_dev);
     s.ready = true;
   }
   *out = &s;
+  return APEX_ATTN_OK;
+}
+
+// A kernel on this device recorded a device-side error (bounded-wait limit, teardown drain
+// limit, shared-memory alignment): every later call fails with
+// APEX_ATTN_ERR_DEVICE_TIMEOUT until apex_attn_device_status() reads and clears the state.
+// The kernel writes the host flag when it records the error, so the first call that
+// starts after that write sees it; no call synchronises for it.
+int sticky_error(const DeviceState& s) {
+  if (s.host_flag != nullptr && *reinterpret_cast<volatile int*>(s.host_flag) != 0)
+    return APEX_ATTN_ERR_DEVICE_TIMEOUT;
   return APEX_ATTN_OK;
 }
 
@@ -273,7 +313,7 @@ struct DeviceGuard {
   }
 };
 
-__global__ void wait_timeout_selftest_kernel(int* status, unsigned long long timeout_ns) {
+__global__ void wait_timeout_selftest_kernel(int* status, int* host_flag, unsigned long long timeout_ns) {
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
   if (threadIdx.x == 0) {
@@ -283,7 +323,7 @@ __global__ void wait_timeout_selftest_kernel(int* status, unsigned long long tim
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const apex::Waiter w{&abort_flag, status, timeout_ns};
+    const apex::Waiter w{&abort_flag, status, timeout_ns, host_flag};
     (void)w.wait(apex::ptx::smem_u32(&bar), 0);  // nothing ever arrives: must time out
   }
   __syncthreads();
@@ -292,8 +332,47 @@ __global__ void wait_timeout_selftest_kernel(int* status, unsigned long long tim
 bool supported_head_dim(int head_dim) { return head_dim == 64 || head_dim == 128 || head_dim == 256; }
 
 int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUtensorMap& mq,
-                        const CUtensorMap& mk, const CUtensorMap& mv, int head_dim, int dtype,
-                        void* stream);
+                        const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap* mo, int head_dim,
+                        int dtype, void* stream);
+
+template <int D, typename T>
+int launch_tile(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
+                const CUtensorMap& mv, const CUtensorMap& mo, const AttnParams& p, int grid, cudaStream_t stream) {
+  auto kern = apex::attn_fwd_tile_kernel<D, T, kEmuTile<D>>;
+  constexpr int smem = apex::TilePlan<D>::kDynamicBytes;
+  if (!(ds.attr_tile & attr_bit)) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_LAUNCH;
+    }
+    ds.attr_tile |= attr_bit;
+  }
+  kern<<<grid, apex::TileCfg<D>::kThreads, smem, stream>>>(mq, mk, mv, mo, p);
+  if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
+  return APEX_ATTN_OK;
+}
+
+// The tile kernel covers batched launches at head dims 64 and 128 without a window; the
+// two-sub-tile kernel covers the rest (d = 256, sliding windows, packed batches). Where
+// both apply, automatic selection follows measurements on one B200 (bf16, causal):
+//   * the tile kernel runs a 128x128 tile slower per SM (0.64x at C2, d = 64; 0.82x at C3,
+//     d = 128: two softmax warps per SM sub-partition hide less latency than four);
+//   * its 128-row items double the parallelism. At d = 128 that wins while the problem
+//     has fewer than 4 x (SM count) 256-row items: B1 H8 N8192 1014 vs 798 TFLOP/s,
+//     B2 H8 N4096 901 vs 696, B1 H32 N1024 266 vs 245, B8 H32 N512 310 vs 279; at 512
+//     items (B2 H16 N4096) the two are level; at 1024 (B2 H16 N8192) the two-sub-tile
+//     kernel is 17 % faster. At d = 64 the tile kernel gains at most 8 % on small shapes
+//     and loses up to 14 %, so automatic selection keeps the two-sub-tile kernel.
+bool use_tile_kernel(int head_dim, const AttnParams& p, const CUtensorMap* mo, int num_sms) {
+  const int kind = g_fwd_kind.load(std::memory_order_relaxed);
+  if (kind == 1 || mo == nullptr || (head_dim != 64 && head_dim != 128) || p.window >= 0 ||
+      p.cu_seqlens != nullptr)
+    return false;
+  if (kind == 2) return true;
+  const long long items = (long long)p.B * p.H * ((p.N + 2 * apex::kBlockM - 1) / (2 * apex::kBlockM));
+  return head_dim == 128 && items < 4LL * num_sms;
+}
 
 // Validation, tensor maps, parameters and dispatch shared by both forward entry points.
 // `noalloc` selects the allocation-free device state and clears its status word first.
@@ -309,8 +388,7 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   if (dtype != APEX_ATTN_BF16 && dtype != APEX_ATTN_FP16) return APEX_ATTN_ERR_UNSUPPORTED_DTYPE;
   if (!std::isfinite(sm_scale) || !(sm_scale > 0.f)) return APEX_ATTN_ERR_BAD_SCALE;
   const long long BH = (long long)batch * heads;
-  const int rows_per_item = item_rows(head_dim);
-  const long long mblocks = (seqlen + rows_per_item - 1) / rows_per_item;
+  const long long mblocks = (seqlen + apex::kBlockM - 1) / apex::kBlockM;  // the smaller item of both kernels
   if (BH * mblocks > 0x7fffffffLL || seqlen > (1 << 30) || BH > (1LL << 30)) return APEX_ATTN_ERR_TOO_LARGE;
   for (int i = 0; i < 12; ++i)
     if (strides[i] < 0 || (strides[i] & 7) != 0 || strides[i] >= (1LL << 38)) return APEX_ATTN_ERR_BAD_LAYOUT;
@@ -326,12 +404,13 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   DeviceGuard guard(dev);
   DeviceState* ds = nullptr;
   int rc = noalloc ? init_device_noalloc(dev, &ds) : init_device(dev, &ds);
-  if (rc != APEX_ATTN_OK) return rc;
+  if (rc != APEX_ATTN_OK || (rc = sticky_error(*ds)) != APEX_ATTN_OK) return rc;
 
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   if ((rc = encode_map(&mq, q, dtype, batch, heads, seqlen, head_dim, strides[0], strides[1], strides[2])) ||
       (rc = encode_map(&mk, k, dtype, batch, heads_kv, seqlen, head_dim, strides[3], strides[4], strides[5])) ||
-      (rc = encode_map(&mv, v, dtype, batch, heads_kv, seqlen, head_dim, strides[6], strides[7], strides[8])))
+      (rc = encode_map(&mv, v, dtype, batch, heads_kv, seqlen, head_dim, strides[6], strides[7], strides[8])) ||
+      (rc = encode_map(&mo, o, dtype, batch, heads, seqlen, head_dim, strides[9], strides[10], strides[11])))
     return rc;
 
   AttnParams p{};
@@ -344,22 +423,25 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   p.H = heads;
   p.N = seqlen;
   p.kv_group = heads / heads_kv;
-  p.window = window;
+  // A window of seqlen or more hides nothing: the unwindowed kernels give the same result.
+  p.window = window < seqlen ? window : -1;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
-  return schedule_and_launch(*ds, noalloc, p, mq, mk, mv, head_dim, dtype, stream);
+  return schedule_and_launch(*ds, noalloc, p, mq, mk, mv, &mo, head_dim, dtype, stream);
 }
 
 // Scheduling parameters, scratch, and the launch shared by every forward entry point. The
 // caller filled the output, shape, mask and scale fields of p.
 int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUtensorMap& mq,
-                        const CUtensorMap& mk, const CUtensorMap& mv, int head_dim, int dtype,
-                        void* stream) {
+                        const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap* mo, int head_dim,
+                        int dtype, void* stream) {
   DeviceState* ds = &dst;
   const long long BH = (long long)p.B * p.H;
-  const int rows_per_item = item_rows(head_dim);
+  const bool tile = use_tile_kernel(head_dim, p, mo, ds->num_sms);
+  const int rows_per_item = tile ? apex::kBlockM : item_rows(head_dim);
   const long long mblocks = (p.N + rows_per_item - 1) / rows_per_item;
   p.status = ds->status;
+  p.host_flag = ds->host_flag_dev;
   p.num_mblocks = (int)mblocks;
   p.num_kblocks = (p.N + apex::kBlockN - 1) / apex::kBlockN;
   p.num_items = (int)(BH * mblocks);
@@ -420,6 +502,13 @@ int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUt
     return APEX_ATTN_ERR_CUDA;
   }
   const bool bf16 = dtype == APEX_ATTN_BF16;
+  if (tile) {
+    if (head_dim == 64)
+      return bf16 ? launch_tile<64, __nv_bfloat16>(*ds, 1u, mq, mk, mv, *mo, p, grid, s)
+                  : launch_tile<64, __half>(*ds, 2u, mq, mk, mv, *mo, p, grid, s);
+    return bf16 ? launch_tile<128, __nv_bfloat16>(*ds, 4u, mq, mk, mv, *mo, p, grid, s)
+                : launch_tile<128, __half>(*ds, 8u, mq, mk, mv, *mo, p, grid, s);
+  }
   switch (head_dim) {
     case 64:
       return bf16 ? launch<64, __nv_bfloat16>(*ds, 1u, mq, mk, mv, p, grid, s)
@@ -465,7 +554,7 @@ int forward_varlen(const apex_attn_varlen_args* a, void* stream) {
   DeviceGuard guard(dev);
   DeviceState* ds = nullptr;
   int rc = init_device(dev, &ds);
-  if (rc != APEX_ATTN_OK) return rc;
+  if (rc != APEX_ATTN_OK || (rc = sticky_error(*ds)) != APEX_ATTN_OK) return rc;
 
   // One 4-D map per tensor over the packed rows: dims (D, total, H, 1).
   const long long* st = a->strides;
@@ -484,12 +573,12 @@ int forward_varlen(const apex_attn_varlen_args* a, void* stream) {
   p.H = a->heads_q;
   p.N = a->max_seqlen;
   p.kv_group = a->heads_q / a->heads_kv;
-  p.window = a->window_left;
+  p.window = a->window_left < a->max_seqlen ? a->window_left : -1;  // wider hides nothing
   p.causal = a->causal ? 1 : 0;
   p.scale_log2 = a->sm_scale * 1.4426950408889634f;
   p.cu_seqlens = a->cu_seqlens;
   p.total = a->total;
-  return schedule_and_launch(*ds, false, p, mq, mk, mv, a->head_dim, a->dtype, stream);
+  return schedule_and_launch(*ds, false, p, mq, mk, mv, nullptr, a->head_dim, a->dtype, stream);
 }
 
 // ------------------------------------------------------------------ backward --
@@ -570,6 +659,7 @@ int launch_bwd(DeviceState& ds, const BwdCall& a, const CUtensorMap& mq, const C
   p.nlse2 = lse2;
   p.ndelta = delta;
   p.status = ds.status;
+  p.host_flag = ds.host_flag_dev;
   p.B = a.batch;
   p.H = a.heads_q;
   p.Hkv = a.heads_kv;
@@ -667,7 +757,7 @@ int backward(const apex_attn_bwd_args* a, void* workspace, size_t workspace_byte
   DeviceGuard guard(dev);
   DeviceState* ds = nullptr;
   int rc = init_device(dev, &ds);
-  if (rc != APEX_ATTN_OK) return rc;
+  if (rc != APEX_ATTN_OK || (rc = sticky_error(*ds)) != APEX_ATTN_OK) return rc;
 
   const long long* st = a->strides;
   const int B = a->batch, H = a->heads_q, HKV = a->heads_kv, N = a->seqlen, D = a->head_dim;
@@ -736,7 +826,7 @@ int backward_varlen(const apex_attn_bwd_varlen_args* a, void* workspace, size_t 
   DeviceGuard guard(dev);
   DeviceState* ds = nullptr;
   int rc = init_device(dev, &ds);
-  if (rc != APEX_ATTN_OK) return rc;
+  if (rc != APEX_ATTN_OK || (rc = sticky_error(*ds)) != APEX_ATTN_OK) return rc;
 
   // Tensor maps over the packed rows: dims (D, total, H, 1); strides are (token, head).
   const long long* st = a->strides;
@@ -790,7 +880,7 @@ const char* apex_attn_strerror(int status) {
     case APEX_ATTN_ERR_UNSUPPORTED_ARCH: return "device is not sm_100 (B200)";
     case APEX_ATTN_ERR_TENSOR_MAP: return "TMA tensor map encoding failed";
     case APEX_ATTN_ERR_LAUNCH: return "kernel launch failed";
-    case APEX_ATTN_ERR_DEVICE_TIMEOUT: return "a kernel reported a device-side error (bounded-wait limit or shared-memory alignment; device status set)";
+    case APEX_ATTN_ERR_DEVICE_TIMEOUT: return "a kernel on this device reported a device-side error (bounded-wait timeout, teardown drain limit or shared-memory alignment); its outputs are incomplete. apex_attn_device_status() reads and clears the state";
     case APEX_ATTN_ERR_TOO_LARGE: return "sizes exceed the supported range";
     case APEX_ATTN_ERR_CUDA: return "CUDA runtime error";
     default: return "unknown status";
@@ -819,6 +909,32 @@ int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, 
                           float sm_scale, const long long* strides, void* stream) {
   return forward(true, q, k, v, o, lse, batch, heads, heads, seqlen, head_dim, dtype, causal, -1,
                  sm_scale, strides, stream);
+}
+
+int apex_attn_noalloc_status(int device, int* flags) {
+  if (!flags) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (device < 0 || device >= kMaxDevices) return APEX_ATTN_ERR_NO_DEVICE;
+  DeviceGuard guard(device);
+  DeviceState* ds = nullptr;
+  int rc = init_device_noalloc(device, &ds);
+  if (rc != APEX_ATTN_OK) return rc;
+  int word = 0;
+  const int zero = 0;
+  // Word 0 of the static scratch is the status word of the allocation-free launches.
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyFromSymbol(&word, g_noalloc_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof(int), 0, cudaMemcpyHostToDevice) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return APEX_ATTN_ERR_CUDA;
+  }
+  *flags = word;
+  return word ? APEX_ATTN_ERR_DEVICE_TIMEOUT : APEX_ATTN_OK;
+}
+
+int apex_attn_set_forward_kernel(int kind) {
+  if (kind < 0 || kind > 2) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  g_fwd_kind.store(kind, std::memory_order_relaxed);
+  return APEX_ATTN_OK;
 }
 
 int apex_attn_num_sms_hint(int device) {
@@ -850,6 +966,7 @@ int apex_attn_device_status(int device, int* flags) {
     (void)cudaGetLastError();
     return APEX_ATTN_ERR_CUDA;
   }
+  *reinterpret_cast<volatile int*>(ds->host_flag) = 0;  // the device is idle: no kernel can set it now
   *flags = host[0];
   return host[0] ? APEX_ATTN_ERR_DEVICE_TIMEOUT : APEX_ATTN_OK;
 }
@@ -865,9 +982,10 @@ int apex_attn_selftest_wait_timeout(int timeout_us, void* stream) {
   int rc = init_device(dev, &ds);
   if (rc != APEX_ATTN_OK) return rc;
   wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      ds->status, (unsigned long long)timeout_us * 1000ull);
+      ds->status, ds->host_flag_dev, (unsigned long long)timeout_us * 1000ull);
   if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
   return APEX_ATTN_OK;
 }
 
 }  // extern "C"
+

@@ -55,6 +55,7 @@ struct AttnParams {
   void* o;
   float* lse;        // nullable, contiguous [B, H, N]
   int* status;       // device status word (bitmask of kStatus*)
+  int* host_flag;    // nullable: mapped pinned host word set to 1 with any status bit
   long long o_sb, o_sh, o_sn;  // output strides in elements (d stride is 1)
   int B, H, N;
   int num_mblocks;   // ceil(N / item rows)
@@ -300,6 +301,17 @@ __device__ __forceinline__ float2 exp2_poly_pair(float2 x) {
   return make_float2(__int_as_float(__float_as_int(pl.x) + ex), __int_as_float(__float_as_int(pl.y) + ey));
 }
 
+// Records a device-side error: the bit goes into the device status word, and a nonzero
+// word into the caller's mapped pinned host flag (when there is one), which the host entry
+// points read before every launch so the next call fails instead of returning quietly.
+__device__ __forceinline__ void report_error(int* status, int* host_flag, int bit) {
+  atomicOr(status, bit);
+  if (host_flag != nullptr) {
+    *reinterpret_cast<volatile int*>(host_flag) = 1;
+    __threadfence_system();
+  }
+}
+
 // Bounded mbarrier wait. Returns false when the CTA is aborting: either another role
 // gave up already, or this wait exceeded the time limit (then it raises the CTA abort
 // flag and the device status bit). Every loop in the kernel is bounded this way so a
@@ -308,6 +320,7 @@ struct Waiter {
   volatile int* abort_flag;
   int* status;
   unsigned long long timeout_ns;
+  int* host_flag;
 
   __device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity) const {
     if (ptx::mbar_try_wait(bar, parity)) return true;
@@ -323,7 +336,7 @@ struct Waiter {
       if (*abort_flag) return false;
       if (ptx::globaltimer_ns() - t0 > timeout_ns) {
         *abort_flag = 1;
-        atomicOr(status, kStatusWaitTimeout);
+        report_error(status, host_flag, kStatusWaitTimeout);
         return false;
       }
     }
@@ -338,12 +351,12 @@ struct Waiter {
 // Wait used only while tearing down: ignores the abort flag, still bounded; a miss is
 // reported through the status word.
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns,
-                                           int* status) {
+                                           int* status, int* host_flag) {
   if (ptx::mbar_try_wait(bar, parity)) return;
   const uint64_t t0 = ptx::globaltimer_ns();
   while (!ptx::mbar_try_wait(bar, parity)) {
     if (ptx::globaltimer_ns() - t0 > limit_ns) {
-      atomicOr(status, kStatusDrainTimeout);
+      report_error(status, host_flag, kStatusDrainTimeout);
       return;
     }
   }
@@ -407,7 +420,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   if (Plan::kDynamicBytes == Plan::kBytes && (raw_addr & 1023u) != 0) {
     // The plan needs the whole 227 KB and the base is not 1 KB aligned: report, do nothing.
-    if (threadIdx.x == 0) atomicOr(p.status, kStatusSmemAlign);
+    if (threadIdx.x == 0) report_error(p.status, p.host_flag, kStatusSmemAlign);
     return;
   }
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
@@ -470,7 +483,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const Waiter W{abort_flag, p.status, p.timeout_ns};
+  const Waiter W{abort_flag, p.status, p.timeout_ns, p.host_flag};
 
   if (warp < kWarpEpi) {
     // =========================================================== softmax ===
@@ -827,7 +840,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       // Every MMA this warp issued (and their commit arrivals) must land before the CTA
       // releases TMEM and shared memory.
       ptx::tc_commit_warp(bar(Plan::kDrain + i));
-      if (lane == 0) drain_wait(bar(Plan::kDrain + i), 0, p.timeout_ns, p.status);
+      if (lane == 0) drain_wait(bar(Plan::kDrain + i), 0, p.timeout_ns, p.status, p.host_flag);
       __syncwarp();
     } else if (warp < kWarpProd + SUB) {
       // ========================================================= producers ===
@@ -906,10 +919,10 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         const int last = fills < NS ? fills : NS;
         for (int k = 0; k < last; ++k) {
           const int f = fills - 1 - k;  // fill index
-          drain_wait(bar(Plan::kKvFull + (f % NS)), (uint32_t)((f / NS) & 1), p.timeout_ns, p.status);
+          drain_wait(bar(Plan::kKvFull + (f % NS)), (uint32_t)((f / NS) & 1), p.timeout_ns, p.status, p.host_flag);
         }
         // qe_par equals the parity of the last Q fill's phase (it flips once per fill).
-        if (q_filled) drain_wait(bar(Plan::kQFull + qi), qe_par, p.timeout_ns, p.status);
+        if (q_filled) drain_wait(bar(Plan::kQFull + qi), qe_par, p.timeout_ns, p.status, p.host_flag);
       }
       __syncwarp();
     }

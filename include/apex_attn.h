@@ -5,12 +5,20 @@
  *   custom_attention_forward(q, k, v, causal=True, sm_scale=None) -> o
  * of mls-bench_fused_attention/fused_attention.py:155-193 (identical copy at
  * submission.py:179-217); apex_attn_bwd adds the backward that training callers need. The Python host module `apex_attn` binds it with ctypes;
- * any other FFI binds the same symbols (see INTEGRATION.md).
+ * any other FFI binds the same symbols.
  *
  * Conventions: all pointers are device pointers on one CUDA device, tensors are
  * logical [B, H, N, D] with unit stride along D, strides are given in elements.
  * Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy default
- * stream). No call allocates caller-visible memory; the library keeps one small
+ * stream).
+ *
+ * Device-side errors are sticky. When a kernel of this library records a device-side
+ * error (a bounded wait expired, so its outputs are incomplete), it also sets a flag in
+ * mapped pinned host memory. Every forward and backward entry point reads that flag
+ * before it launches anything and returns APEX_ATTN_ERR_DEVICE_TIMEOUT while it is set,
+ * until apex_attn_device_status() reads and clears the device's state. No call
+ * synchronises for this: the first call that starts after the failing kernel wrote the
+ * flag reports it (the allocation-free entry point has its own reader, below). No call allocates caller-visible memory; the library keeps one small
  * scratch buffer per device (a status word for device-side error reporting and the
  * work-item counters of its scheduler).
  */
@@ -34,7 +42,7 @@ extern "C" {
 #define APEX_ATTN_ERR_UNSUPPORTED_ARCH -7   /* device is not sm_100 */
 #define APEX_ATTN_ERR_TENSOR_MAP -8         /* cuTensorMapEncodeTiled rejected a tensor */
 #define APEX_ATTN_ERR_LAUNCH -9             /* kernel launch failed */
-#define APEX_ATTN_ERR_DEVICE_TIMEOUT -10    /* a kernel hit its bounded-wait limit */
+#define APEX_ATTN_ERR_DEVICE_TIMEOUT -10    /* a kernel hit its bounded-wait limit (sticky, below) */
 #define APEX_ATTN_ERR_TOO_LARGE -11         /* sizes exceed the supported range */
 #define APEX_ATTN_ERR_CUDA -12              /* other CUDA runtime error */
 
@@ -133,8 +141,24 @@ typedef struct apex_attn_varlen_args {
 int apex_attn_fwd_varlen(const apex_attn_varlen_args* args, void* stream);
 
 /*
+ * Selects the forward kernel for later calls in this process (all devices):
+ *   0  automatic (default): for batched calls at head dims 64 and 128 without a window,
+ *      whichever of the two kernels has the shorter estimated makespan: the tile kernel
+ *      (one 128-row query tile per CTA, S and P double-buffered in tensor memory,
+ *      TMA-store epilogue) for problems too small to fill the GPU with 256-row items,
+ *      else the two-sub-tile kernel; the two-sub-tile kernel for every other call;
+ *   1  the two-sub-tile kernel for every call;
+ *   2  the tile kernel wherever it applies (batched, head dim 64 or 128, no window).
+ * Both kernels compute the same function within the stated tolerances; this exists to
+ * measure them against each other. Returns APEX_ATTN_ERR_INVALID_ARGUMENT for other values.
+ * No counterpart in the reference (its _CONFIGS table picks one kernel per head dim,
+ * fused_attention.py:148-152).
+ */
+int apex_attn_set_forward_kernel(int kind);
+
+/*
  * Reads and clears the device status word of `device` after synchronising that
- * device. *flags receives the raw bits (1 = a kernel hit its bounded-wait limit,
+ * device, and clears the sticky host flag. *flags receives the raw bits (1 = a kernel hit its bounded-wait limit,
  * 2 = a copy or MMA still in flight at kernel teardown did not land within the limit,
  * 4 = the dynamic shared-memory base was not 1 KB aligned, so a kernel did nothing).
  * Returns APEX_ATTN_ERR_DEVICE_TIMEOUT when any bit was set.
@@ -169,13 +193,24 @@ int apex_attn_selftest_wait_timeout(int timeout_us, void* stream);
  * Each call clears the status word and its counter on `stream` before its kernel. All
  * calls share the array: calls that overlap on the GPU (other streams, other threads)
  * race on the status word, and on a counter once more than 32 calls are in flight. A
- * bounded wait that expires still ends the kernel early, but its status bit stays in the
- * shared scratch, which apex_attn_device_status does not read; callers that need
- * device-fault reports use apex_attn_fwd.
+ * bounded wait that expires still ends the kernel early; its status bit stays in the
+ * shared scratch until the next allocation-free call clears it, and only
+ * apex_attn_noalloc_status reads it (apex_attn_device_status does not). This path keeps
+ * no sticky host flag, since that needs pinned host memory.
  */
 int apex_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
                           int batch, int heads, int seqlen, int head_dim, int dtype, int causal,
                           float sm_scale, const long long* strides, void* stream);
+
+/*
+ * Reads and clears the status word that apex_attn_fwd_noalloc launches on `device` share,
+ * after synchronising the device; allocates nothing. *flags receives the bits described
+ * for apex_attn_device_status; returns APEX_ATTN_ERR_DEVICE_TIMEOUT when any was set. The
+ * word holds only what happened since the last allocation-free call began (each call
+ * clears it before its kernel), so read it after the call whose outcome matters and
+ * before the next one. No counterpart in the reference.
+ */
+int apex_attn_noalloc_status(int device, int* flags);
 
 /*
  * Backward of the attention computed by apex_attn_fwd / apex_attn_fwd_ex:

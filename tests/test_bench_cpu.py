@@ -42,3 +42,31 @@ def test_reference_arm_other_ranks_print_nothing():
                   extra_env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def _contract_line(r):
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    return json.loads(lines[0])
+
+
+def test_reference_arm_config_is_the_gpu_arms():
+    """Both arms describe the same workload with the same config dict, so a driver can
+    pair their lines; the reference line also gives ms_per_step for the whole workload."""
+    sys.path.insert(0, ROOT)
+    import bench
+    d = _contract_line(run_bench(["--impl", "reference", "--steps", "1", "--cpu-budget", "2"]))
+    assert d["config"] == bench.config_single()
+    assert d["ms_per_step"] > 0
+
+
+def test_torchrun_world_one_times_the_c5_slice():
+    """Under torchrun every WORLD_SIZE, 1 included, times 64 C5 heads per rank, so a 1->8
+    scaling run divides like by like (the reference arm follows the same rule)."""
+    sys.path.insert(0, ROOT)
+    import bench
+    d = _contract_line(run_bench(["--impl", "reference", "--steps", "1", "--cpu-budget", "2"],
+                                 extra_env={"RANK": "0", "WORLD_SIZE": "1", "LOCAL_RANK": "0"}))
+    assert d["config"] == bench.config_multi(1) and d["n_gpus"] == 1
+    assert "C5 slice" in d["config"]["workload"]
