@@ -488,171 +488,335 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
   if (warp < kWarpEpi) {
     // =========================================================== softmax ===
     ptx::setmaxnreg_inc<C::kRegsSoftmax>();
-    constexpr int kCols = kBlockN / CS;  // key columns of the tile this warpgroup handles
-    constexpr int NH = kCols / 64;       // 64-key halves among them
-    const int i = (warp >> 2) / CS;     // sub-tile
-    const int cs = (warp >> 2) % CS;    // column part: keys [cs * kCols, (cs + 1) * kCols)
-    const int quarter = warp & 3;       // TMEM lane quarter
-    const int r = quarter * 32 + lane;  // row within the sub-tile
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128 + cs * kCols);
-    const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
-    const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64 + cs * (kCols / 2));
-    float* xch = reinterpret_cast<float*>(smem + Plan::kXch);  // [SUB][CS][2][128]
-    int tcount = 0;  // tiles this warpgroup processed (row-max exchange slot and parity)
-    // Row r of P in shared memory: two 16 KB chunks (keys 0-63, 64-127) of the SW128
-    // K-major layout; 16-byte unit u of the row sits at unit position u ^ (r & 7).
-    const uint32_t sP = sbase + Plan::kP + i * Plan::kPTileBytes + r * 128;
-    const float c = p.scale_log2;
-    const float2 c2 = make_float2(c, c);
-    uint32_t s_par = 0, le_par = 1, pf_par = 0;
-    int p_written = 0;  // P tiles handed over so far (the buffer is reused every tile)
-    bool ok = true;
-    ItemReader reader;
-    while (ok) {
-      int t;
-      if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
-      const WorkItem it = decode_item<SUB, WIN, VAR>(t, p);
-      const int nb = it.nbi(i);
-      const int lo = it.loi(i);
-      if (nb == 0) continue;
-      const int r0 = it.m0 + i * kBlockM;  // first row of the sub-tile
-      const int diag = r0 / kBlockN;
-      float m = 0.f, l = 0.f;
-      for (int j = lo; j < nb; ++j) {
-        if (!(ok = W.wait_warp(bar(Plan::kSFull + i), s_par))) break;
-        s_par ^= 1;
-        ptx::tc_fence_after();
-        float s[kCols];
-        {
-          uint32_t v[kCols / 32][32];
-#pragma unroll
-          for (int ch = 0; ch < kCols / 32; ++ch) ptx::tmem_ld32(tS + ch * 32, v[ch]);
+    if constexpr (CS == 2 && !WIN) {
+      // Two warpgroups per sub-tile split its rows: in each 32-lane TMEM quarter, the warp
+      // of warpgroup h takes lanes 16h .. 16h + 15 (16-lane tcgen05.ld/st shapes), all 128
+      // keys of the tile. Thread t holds rows ra = lb + t/4 and ra + 8, keys 8e + kq + {0,1}
+      // (e = 0..15, kq = 2 (t % 4)); the four threads of a row reduce its max with two
+      // shuffles. The warpgroups never exchange anything, so neither waits for the other:
+      // C2 and the fp16 MLS d=64 shape +4.5 % over splitting the keys with a per-tile row-max
+      // exchange (measured alternating builds). Windowed launches keep the key split below:
+      // the per-row window bounds push this form past its 88-register budget (spills,
+      // -14 %).
+      const int i = (warp >> 2) >> 1;                     // sub-tile
+      const int lb = (warp & 3) * 32 + ((warp >> 2) & 1) * 16;  // first TMEM lane (= row) of this warp
+      const int ra = lb + (lane >> 2);
+      const int kq = 2 * (lane & 3);
+      const uint32_t lane_off = (uint32_t)lb << 16;
+      const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128);
+      const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
+      const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64);
+      static_assert(D == 64, "the row-split softmax rescales O in one 64-column block");
+      const float c = p.scale_log2;
+      const float2 c2 = make_float2(c, c);
+      uint32_t s_par = 0, le_par = 1, pf_par = 0;
+      int p_written = 0;  // P tiles handed over so far (the buffer is reused every tile)
+      bool ok = true;
+      ItemReader reader;
+      while (ok) {
+        int t;
+        if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
+        const WorkItem it = decode_item<SUB, WIN, VAR>(t, p);
+        const int nb = it.nbi(i);
+        const int lo = it.loi(i);
+        if (nb == 0) continue;
+        const int r0 = it.m0 + i * kBlockM;  // first row of the sub-tile
+        const int diag = r0 / kBlockN;
+        float m[2] = {0.f, 0.f}, l[2] = {0.f, 0.f};  // rows ra, ra + 8
+        for (int j = lo; j < nb; ++j) {
+          if (!(ok = W.wait_warp(bar(Plan::kSFull + i), s_par))) break;
+          s_par ^= 1;
+          ptx::tc_fence_after();
+          // v[h][4i' + 2rr + b] = S(row ra + 8 rr, key 8e + kq + b), e = 8h + i'
+          uint32_t v[2][32];
+          ptx::tmem_ld_16x256b_x8(tS, v[0]);
+          ptx::tmem_ld_16x256b_x8(tS + 64, v[1]);
           ptx::tmem_wait_ld();
+          ptx::reg_fence32(v[0]);
+          ptx::reg_fence32(v[1]);
+          // S is in registers: the MMA warp may overwrite it with the next tile's scores.
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(bar(Plan::kSFree + i));
+          const bool diag_tile = p.causal && j == diag;
+          const int kv_last_valid = it.len - (it.nkb - 1) * kBlockN;  // keys in the last K tile
+          const bool tail_tile = !p.causal && j == it.nkb - 1 && kv_last_valid < kBlockN;
+          const bool masked = diag_tile || tail_tile;  // warp-uniform
+          if (masked) {
 #pragma unroll
-          for (int ch = 0; ch < kCols / 32; ++ch) {
-            ptx::reg_fence32(v[ch]);  // no use of the loaded values above the wait
+            for (int rr = 0; rr < 2; ++rr) {
+              const int row = ra + 8 * rr;
+              const int limit = diag_tile ? row + 1 : kv_last_valid;  // keys >= limit are masked
 #pragma unroll
-            for (int e = 0; e < 32; ++e) s[ch * 32 + e] = __uint_as_float(v[ch][e]);
+              for (int e = 0; e < 16; ++e)
+#pragma unroll
+                for (int b = 0; b < 2; ++b)
+                  if (8 * e + kq + b >= limit) v[e >> 3][4 * (e & 7) + 2 * rr + b] = __float_as_uint(-INFINITY);
+            }
           }
-        }
-        // S is in registers: the MMA warp may overwrite it with the next tile's scores.
-        ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(Plan::kSFree + i));
-        const bool diag_tile = p.causal && j == diag;
-        const int kv_last_valid = it.len - (it.nkb - 1) * kBlockN;  // keys in the last K tile
-        const bool tail_tile = !p.causal && j == it.nkb - 1 && kv_last_valid < kBlockN;
-        // Sliding window: the tile holds keys below some row's window start iff its first
-        // key is below the sub-tile's last row minus the window.
-        const bool win_tile = WIN && j * kBlockN < r0 + kBlockM - 1 - p.window;
-        const bool masked = diag_tile || tail_tile || win_tile;  // warp-uniform
-        if (masked) {
-          const int kv_limit = diag_tile ? r + 1 : (tail_tile ? kv_last_valid : kBlockN);  // keys >= limit masked
-          const int kv_first = win_tile ? r0 + r - p.window - j * kBlockN : 0;            // keys < first masked
+          bool resc = false;
+          float alpha[2] = {1.f, 1.f};
+          float2 nm2[2];
 #pragma unroll
-          for (int e = 0; e < kCols; ++e)
-            if (e + cs * kCols >= kv_limit || e + cs * kCols < kv_first) s[e] = -INFINITY;
-        }
-        float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
-        float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
-        static_assert(kBlockN % 8 == 0, "row max consumes 8 scores per step");
+          for (int rr = 0; rr < 2; ++rr) {
+            float m0 = fmaxf(__uint_as_float(v[0][2 * rr]), __uint_as_float(v[0][2 * rr + 1]));
+            float m1 = fmaxf(__uint_as_float(v[1][2 * rr]), __uint_as_float(v[1][2 * rr + 1]));
 #pragma unroll
-        for (int e = 8; e < kCols; e += 8) {
-          mx0 = ptx::fmax3(mx0, s[e], s[e + 1]);
-          mx1 = ptx::fmax3(mx1, s[e + 2], s[e + 3]);
-          mx2 = ptx::fmax3(mx2, s[e + 4], s[e + 5]);
-          mx3 = ptx::fmax3(mx3, s[e + 6], s[e + 7]);
-        }
-        float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;  // log2 domain
-        if (CS == 2) {
-          // Row max over the whole tile: publish this part's max, take the partner's. Slots
-          // alternate by tile; a slot is rewritten two tiles later, after the partner has
-          // read it (it reads tile t before it can reach the exchange of tile t + 1).
-          const int slot = tcount & 1;
-          xch[((i * CS + cs) * 2 + slot) * kBlockM + r] = mx;
-          ptx::mbar_arrive(bar(Plan::kMaxX + i * CS + cs));
-          if (!(ok = W.wait_warp(bar(Plan::kMaxX + i * CS + (1 - cs)), (uint32_t)slot))) break;
-          mx = fmaxf(mx, xch[((i * CS + (1 - cs)) * 2 + slot) * kBlockM + r]);
-        }
-        ++tcount;
-        float alpha = 1.f;
-        bool resc = false;
-        if (j == lo) {
-          m = mx;  // -inf when the window hides this whole tile from the row
-        } else if (mx > m + kRescaleLog2) {  // from m = -inf: alpha = 0, as it must be
-          alpha = ptx::ex2(m - mx);
-          m = mx;
-          resc = true;
-        }
-        l *= alpha;
-        // p = exp2(s*c - m), packed to 16-bit pairs: pk[key half][32]
-        const float m_use = (WIN && m == -INFINITY) ? 0.f : m;  // all keys masked: p = 0, not NaN
-        const float2 nm2 = make_float2(-m_use, -m_use);
-        float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
-        uint32_t pk[NH][32];
-        auto exp_half = [&](const int half, auto poly) {
-          constexpr bool kPoly = decltype(poly)::value;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float2 x = __ffma2_rn(make_float2(s[half * 64 + 2 * e], s[half * 64 + 2 * e + 1]), c2, nm2);
-            float2 pr;
-            if (kPoly && (e & 7) < EMU8) pr = exp2_poly_pair(x);
-            else pr = make_float2(ptx::ex2(x.x), ptx::ex2(x.y));
-            if (e & 1) sb = __fadd2_rn(sb, pr);
-            else sa = __fadd2_rn(sa, pr);
-            pk[half][e] = DType<T>::pack(pr.x, pr.y);
+            for (int e = 1; e < 8; ++e) {
+              m0 = ptx::fmax3(m0, __uint_as_float(v[0][4 * e + 2 * rr]), __uint_as_float(v[0][4 * e + 2 * rr + 1]));
+              m1 = ptx::fmax3(m1, __uint_as_float(v[1][4 * e + 2 * rr]), __uint_as_float(v[1][4 * e + 2 * rr + 1]));
+            }
+            float mx = fmaxf(m0, m1);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // the four threads of the row
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            mx *= c;  // log2 domain
+            if (j == lo) {
+              m[rr] = mx;
+            } else if (mx > m[rr] + kRescaleLog2) {
+              alpha[rr] = ptx::ex2(m[rr] - mx);
+              m[rr] = mx;
+              resc = true;
+            }
+            l[rr] *= alpha[rr];
+            nm2[rr] = make_float2(-m[rr], -m[rr]);
           }
-        };
+          // p = exp2(s c - m), packed to 16-bit pairs in the 16x128b store layout:
+          // pk[2e + rr] = P(row ra + 8 rr, keys 8e + kq, 8e + kq + 1)
+          uint32_t pk[32];
+          float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+          auto exps = [&](auto poly) {
+            constexpr bool kPoly = decltype(poly)::value;
 #pragma unroll
-        for (int h = 0; h < NH; ++h) {
-          if (masked) exp_half(h, std::false_type{});  // masked keys hold -inf: MUFU gives exactly 0
-          else exp_half(h, std::integral_constant<bool, (EMU8 > 0)>{});
-        }
-        const float2 sum = __fadd2_rn(sa, sb);
-        l += sum.x + sum.y;
-        // The P buffer and O are free once the previous P.V of this sub-tile completed.
-        if (p_written > 0) {
-          if (!(ok = W.wait_warp(bar(Plan::kPFree + i), pf_par))) break;
-          pf_par ^= 1;
-        }
-        ++p_written;
-        ptx::tc_fence_after();
-        if (__any_sync(0xffffffffu, resc)) {
-          // O is quiescent: the previous P.V completed (above) and the next waits for P.
-#pragma unroll 1
-          for (int ch = cs * (D / 32 / CS); ch < (cs + 1) * (D / 32 / CS); ++ch) {  // this part's O columns
-            uint32_t v[32];
-            ptx::tmem_ld32(tO + ch * 32, v);
+            for (int e = 0; e < 16; ++e) {
+#pragma unroll
+              for (int rr = 0; rr < 2; ++rr) {
+                const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[e >> 3][4 * (e & 7) + 2 * rr]),
+                                                        __uint_as_float(v[e >> 3][4 * (e & 7) + 2 * rr + 1])),
+                                            c2, nm2[rr]);
+                float2 pr;
+                if (kPoly && ((2 * e + rr) & 7) < EMU8) pr = exp2_poly_pair(x);
+                else pr = make_float2(ptx::ex2(x.x), ptx::ex2(x.y));
+                acc[rr] = __fadd2_rn(acc[rr], pr);
+                pk[2 * e + rr] = DType<T>::pack(pr.x, pr.y);
+              }
+            }
+          };
+          if (masked) exps(std::false_type{});  // masked keys hold -inf: MUFU gives exactly 0
+          else exps(std::integral_constant<bool, (EMU8 > 0)>{});
+          l[0] += acc[0].x + acc[0].y;
+          l[1] += acc[1].x + acc[1].y;
+          // The P buffer and O are free once the previous P.V of this sub-tile completed.
+          if (p_written > 0) {
+            if (!(ok = W.wait_warp(bar(Plan::kPFree + i), pf_par))) break;
+            pf_par ^= 1;
+          }
+          ++p_written;
+          ptx::tc_fence_after();
+          if (__any_sync(0xffffffffu, resc)) {
+            // O is quiescent: the previous P.V completed (above) and the next waits for P.
+            uint32_t o[32];
+            ptx::tmem_ld_16x256b_x8(tO, o);
             ptx::tmem_wait_ld();
-            ptx::reg_fence32(v);
+            ptx::reg_fence32(o);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            ptx::tmem_st32(tO + ch * 32, v);
+            for (int e = 0; e < 8; ++e) {
+              o[4 * e] = __float_as_uint(__uint_as_float(o[4 * e]) * alpha[0]);
+              o[4 * e + 1] = __float_as_uint(__uint_as_float(o[4 * e + 1]) * alpha[0]);
+              o[4 * e + 2] = __float_as_uint(__uint_as_float(o[4 * e + 2]) * alpha[1]);
+              o[4 * e + 3] = __float_as_uint(__uint_as_float(o[4 * e + 3]) * alpha[1]);
+            }
+            ptx::tmem_st_16x256b_x8(tO, o);
+          }
+          ptx::tmem_st_16x128b_x16(tP, pk);
+          ptx::tmem_wait_st();
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(bar(Plan::kPFull + i));
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {  // the row's sum over its four threads
+          l[rr] += __shfl_xor_sync(0xffffffffu, l[rr], 1);
+          l[rr] += __shfl_xor_sync(0xffffffffu, l[rr], 2);
+        }
+        if (!(ok = W.wait_warp(bar(Plan::kLEmpty + i), le_par))) break;
+        le_par ^= 1;
+        if ((lane & 3) == 0) {
+          // Full row sums in the first slot; the epilogue adds both slots.
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            row_l[(i * CS) * kBlockM + ra + 8 * rr] = l[rr];
+            row_l[(i * CS + 1) * kBlockM + ra + 8 * rr] = 0.f;
+            row_m[i * kBlockM + ra + 8 * rr] = m[rr];
           }
         }
-        if (C::kPInTmem) {
-#pragma unroll
-          for (int h = 0; h < NH; ++h) ptx::tmem_st32(tP + h * 32, pk[h]);
-          ptx::tmem_wait_st();
-        } else {
-#pragma unroll
-          for (int h = 0; h < NH; ++h)
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              ptx::st_shared_v4(sP + h * Plan::kChunkBytes + ((u ^ (r & 7)) << 4), pk[h][4 * u],
-                                pk[h][4 * u + 1], pk[h][4 * u + 2], pk[h][4 * u + 3]);
-          ptx::fence_proxy_async_smem();
-          ptx::tmem_wait_st();  // the O rescale stores, if any
-        }
-        ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(Plan::kPFull + i));
+        ptx::mbar_arrive(bar(Plan::kLFull + i));
       }
-      if (!ok) break;
-      if (!(ok = W.wait_warp(bar(Plan::kLEmpty + i), le_par))) break;
-      le_par ^= 1;
-      row_l[(i * CS + cs) * kBlockM + r] = l;  // this part's share of the row sum
-      if (cs == 0) row_m[i * kBlockM + r] = m;
-      ptx::mbar_arrive(bar(Plan::kLFull + i));
+    } else {
+      constexpr int kCols = kBlockN / CS;  // key columns of the tile this warpgroup handles
+      constexpr int NH = kCols / 64;       // 64-key halves among them
+      const int i = (warp >> 2) / CS;     // sub-tile
+      const int cs = (warp >> 2) % CS;    // column part: keys [cs * kCols, (cs + 1) * kCols)
+      const int quarter = warp & 3;       // TMEM lane quarter
+      const int r = quarter * 32 + lane;  // row within the sub-tile
+      const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+      const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128 + cs * kCols);
+      const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
+      const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64 + cs * (kCols / 2));
+      float* xch = reinterpret_cast<float*>(smem + Plan::kXch);  // [SUB][CS][2][128]
+      int tcount = 0;  // tiles this warpgroup processed (row-max exchange slot and parity)
+      // Row r of P in shared memory: two 16 KB chunks (keys 0-63, 64-127) of the SW128
+      // K-major layout; 16-byte unit u of the row sits at unit position u ^ (r & 7).
+      const uint32_t sP = sbase + Plan::kP + i * Plan::kPTileBytes + r * 128;
+      const float c = p.scale_log2;
+      const float2 c2 = make_float2(c, c);
+      uint32_t s_par = 0, le_par = 1, pf_par = 0;
+      int p_written = 0;  // P tiles handed over so far (the buffer is reused every tile)
+      bool ok = true;
+      ItemReader reader;
+      while (ok) {
+        int t;
+        if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
+        const WorkItem it = decode_item<SUB, WIN, VAR>(t, p);
+        const int nb = it.nbi(i);
+        const int lo = it.loi(i);
+        if (nb == 0) continue;
+        const int r0 = it.m0 + i * kBlockM;  // first row of the sub-tile
+        const int diag = r0 / kBlockN;
+        float m = 0.f, l = 0.f;
+        for (int j = lo; j < nb; ++j) {
+          if (!(ok = W.wait_warp(bar(Plan::kSFull + i), s_par))) break;
+          s_par ^= 1;
+          ptx::tc_fence_after();
+          float s[kCols];
+          {
+            uint32_t v[kCols / 32][32];
+  #pragma unroll
+            for (int ch = 0; ch < kCols / 32; ++ch) ptx::tmem_ld32(tS + ch * 32, v[ch]);
+            ptx::tmem_wait_ld();
+  #pragma unroll
+            for (int ch = 0; ch < kCols / 32; ++ch) {
+              ptx::reg_fence32(v[ch]);  // no use of the loaded values above the wait
+  #pragma unroll
+              for (int e = 0; e < 32; ++e) s[ch * 32 + e] = __uint_as_float(v[ch][e]);
+            }
+          }
+          // S is in registers: the MMA warp may overwrite it with the next tile's scores.
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(bar(Plan::kSFree + i));
+          const bool diag_tile = p.causal && j == diag;
+          const int kv_last_valid = it.len - (it.nkb - 1) * kBlockN;  // keys in the last K tile
+          const bool tail_tile = !p.causal && j == it.nkb - 1 && kv_last_valid < kBlockN;
+          // Sliding window: the tile holds keys below some row's window start iff its first
+          // key is below the sub-tile's last row minus the window.
+          const bool win_tile = WIN && j * kBlockN < r0 + kBlockM - 1 - p.window;
+          const bool masked = diag_tile || tail_tile || win_tile;  // warp-uniform
+          if (masked) {
+            const int kv_limit = diag_tile ? r + 1 : (tail_tile ? kv_last_valid : kBlockN);  // keys >= limit masked
+            const int kv_first = win_tile ? r0 + r - p.window - j * kBlockN : 0;            // keys < first masked
+  #pragma unroll
+            for (int e = 0; e < kCols; ++e)
+              if (e + cs * kCols >= kv_limit || e + cs * kCols < kv_first) s[e] = -INFINITY;
+          }
+          float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+          float mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
+          static_assert(kBlockN % 8 == 0, "row max consumes 8 scores per step");
+  #pragma unroll
+          for (int e = 8; e < kCols; e += 8) {
+            mx0 = ptx::fmax3(mx0, s[e], s[e + 1]);
+            mx1 = ptx::fmax3(mx1, s[e + 2], s[e + 3]);
+            mx2 = ptx::fmax3(mx2, s[e + 4], s[e + 5]);
+            mx3 = ptx::fmax3(mx3, s[e + 6], s[e + 7]);
+          }
+          float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;  // log2 domain
+          if (CS == 2) {
+            // Row max over the whole tile: publish this part's max, take the partner's. Slots
+            // alternate by tile; a slot is rewritten two tiles later, after the partner has
+            // read it (it reads tile t before it can reach the exchange of tile t + 1).
+            const int slot = tcount & 1;
+            xch[((i * CS + cs) * 2 + slot) * kBlockM + r] = mx;
+            ptx::mbar_arrive(bar(Plan::kMaxX + i * CS + cs));
+            if (!(ok = W.wait_warp(bar(Plan::kMaxX + i * CS + (1 - cs)), (uint32_t)slot))) break;
+            mx = fmaxf(mx, xch[((i * CS + (1 - cs)) * 2 + slot) * kBlockM + r]);
+          }
+          ++tcount;
+          float alpha = 1.f;
+          bool resc = false;
+          if (j == lo) {
+            m = mx;  // -inf when the window hides this whole tile from the row
+          } else if (mx > m + kRescaleLog2) {  // from m = -inf: alpha = 0, as it must be
+            alpha = ptx::ex2(m - mx);
+            m = mx;
+            resc = true;
+          }
+          l *= alpha;
+          // p = exp2(s*c - m), packed to 16-bit pairs: pk[key half][32]
+          const float m_use = (WIN && m == -INFINITY) ? 0.f : m;  // all keys masked: p = 0, not NaN
+          const float2 nm2 = make_float2(-m_use, -m_use);
+          float2 sa = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
+          uint32_t pk[NH][32];
+          auto exp_half = [&](const int half, auto poly) {
+            constexpr bool kPoly = decltype(poly)::value;
+  #pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float2 x = __ffma2_rn(make_float2(s[half * 64 + 2 * e], s[half * 64 + 2 * e + 1]), c2, nm2);
+              float2 pr;
+              if (kPoly && (e & 7) < EMU8) pr = exp2_poly_pair(x);
+              else pr = make_float2(ptx::ex2(x.x), ptx::ex2(x.y));
+              if (e & 1) sb = __fadd2_rn(sb, pr);
+              else sa = __fadd2_rn(sa, pr);
+              pk[half][e] = DType<T>::pack(pr.x, pr.y);
+            }
+          };
+  #pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            if (masked) exp_half(h, std::false_type{});  // masked keys hold -inf: MUFU gives exactly 0
+            else exp_half(h, std::integral_constant<bool, (EMU8 > 0)>{});
+          }
+          const float2 sum = __fadd2_rn(sa, sb);
+          l += sum.x + sum.y;
+          // The P buffer and O are free once the previous P.V of this sub-tile completed.
+          if (p_written > 0) {
+            if (!(ok = W.wait_warp(bar(Plan::kPFree + i), pf_par))) break;
+            pf_par ^= 1;
+          }
+          ++p_written;
+          ptx::tc_fence_after();
+          if (__any_sync(0xffffffffu, resc)) {
+            // O is quiescent: the previous P.V completed (above) and the next waits for P.
+  #pragma unroll 1
+            for (int ch = cs * (D / 32 / CS); ch < (cs + 1) * (D / 32 / CS); ++ch) {  // this part's O columns
+              uint32_t v[32];
+              ptx::tmem_ld32(tO + ch * 32, v);
+              ptx::tmem_wait_ld();
+              ptx::reg_fence32(v);
+  #pragma unroll
+              for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+              ptx::tmem_st32(tO + ch * 32, v);
+            }
+          }
+          if (C::kPInTmem) {
+  #pragma unroll
+            for (int h = 0; h < NH; ++h) ptx::tmem_st32(tP + h * 32, pk[h]);
+            ptx::tmem_wait_st();
+          } else {
+  #pragma unroll
+            for (int h = 0; h < NH; ++h)
+  #pragma unroll
+              for (int u = 0; u < 8; ++u)
+                ptx::st_shared_v4(sP + h * Plan::kChunkBytes + ((u ^ (r & 7)) << 4), pk[h][4 * u],
+                                  pk[h][4 * u + 1], pk[h][4 * u + 2], pk[h][4 * u + 3]);
+            ptx::fence_proxy_async_smem();
+            ptx::tmem_wait_st();  // the O rescale stores, if any
+          }
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(bar(Plan::kPFull + i));
+        }
+        if (!ok) break;
+        if (!(ok = W.wait_warp(bar(Plan::kLEmpty + i), le_par))) break;
+        le_par ^= 1;
+        row_l[(i * CS + cs) * kBlockM + r] = l;  // this part's share of the row sum
+        if (cs == 0) row_m[i * kBlockM + r] = m;
+        ptx::mbar_arrive(bar(Plan::kLFull + i));
+      }
     }
   } else if (warp < kWarpMma) {
     // ========================================================== epilogue ===
