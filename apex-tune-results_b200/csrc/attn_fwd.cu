@@ -261,7 +261,7 @@ template <int D, typename T, bool WIN, bool VAR>
 int launch_one(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
                const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
   auto kern = apex::attn_fwd_sm100_kernel<D, T, kEmu<D>, WIN, VAR>;
-  constexpr int smem = apex::SmemPlan<D>::kDynamicBytes;
+  constexpr int smem = apex::SmemPlan<D, WIN>::kDynamicBytes;
   if (!(ds.attr_done & attr_bit)) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
@@ -270,7 +270,7 @@ int launch_one(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const 
     }
     ds.attr_done |= attr_bit;
   }
-  kern<<<grid, apex::Cfg<D>::kThreads, smem, stream>>>(mq, mk, mv, p);
+  kern<<<grid, apex::Cfg<D, WIN>::kThreads, smem, stream>>>(mq, mk, mv, p);
   if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
   return APEX_ATTN_OK;
 }

@@ -81,16 +81,28 @@ struct AttnParams {
 #ifndef APEX_FWD_CS64
 #define APEX_FWD_CS64 2
 #endif
+// Row-split softmax at d = 128 too (two warpgroups per sub-tile, P stored to shared memory
+// by 4-byte words). Off: measured level with one warpgroup per sub-tile (fp16 MLS d128
+// 1164 vs 1164 TFLOP/s, C3 within noise), so d = 128 is not limited by softmax latency.
+#ifndef APEX_FWD_ROWSPLIT128
+#define APEX_FWD_ROWSPLIT128 0
+#endif
 
-template <int D>
+// WIN: the configuration of windowed launches (see kCS).
+template <int D, bool WIN = false>
 struct Cfg {
   static_assert(D == 64 || D == 128 || D == 256, "head dims 64, 128, 256");
   static constexpr int kSub = D == 256 ? 1 : 2;          // 128-row query sub-tiles per item
-  // Softmax warpgroups per sub-tile: each takes kBlockN / kCS of the tile's key columns for
-  // all 128 rows (row max exchanged through shared memory, row sums added in the
-  // epilogue). Two per sub-tile put four softmax warps on every SM sub-partition, so
-  // one warp's loads, row max and P store overlap another's exponentials.
-  static constexpr int kCS = D == 64 ? APEX_FWD_CS64 : 1;
+  // Softmax warpgroups per sub-tile. Two per sub-tile put four softmax warps on every SM
+  // sub-partition, so one warp's loads, row max and P store overlap another's
+  // exponentials. Unwindowed launches split the sub-tile's rows between the two (kRowSplit:
+  // 16-lane TMEM shapes, nothing exchanged); windowed ones split its key columns, with the
+  // row max exchanged through shared memory and the row sums added in the epilogue (the
+  // per-row window bounds do not fit the row split's register budget). The key split needs
+  // P in TMEM, so windowed d = 128 launches keep one warpgroup per sub-tile.
+  static constexpr int kCS = D == 64 ? APEX_FWD_CS64 : ((D == 128 && !WIN && APEX_FWD_ROWSPLIT128) ? 2 : 1);
+  static constexpr bool kRowSplit = kCS == 2 && !WIN;
+  static constexpr int kLSlots = kCS == 2 && !kRowSplit ? 2 : 1;  // row-sum slots per sub-tile
   static constexpr bool kPInTmem = D != 128;             // else P lives in shared memory
   static constexpr int kParts = D == 256 ? 2 : 1;        // ring stages per K or V tile
   static constexpr int kStageCols = D / kParts;          // head-dim columns per stage
@@ -103,13 +115,13 @@ struct Cfg {
   // setmaxnreg budgets (multiples of 8): softmax, epilogue, the remaining warpgroup. Their
   // sum x 128 must not exceed the launch allocation (kThreads x (65536 / kThreads)), or
   // setmaxnreg.inc would wait forever; checked below.
-  static constexpr int kRegsSoftmax = kCS == 2 ? 88 : (kSub == 2 ? 184 : 240);
-  static constexpr int kRegsEpilogue = kCS == 2 ? 64 : (kSub == 2 ? 80 : 128);
-  static constexpr int kRegsOther = kCS == 2 ? 48 : (kSub == 2 ? 56 : 136);
+  static constexpr int kRegsSoftmax = kCS == 2 ? (D == 128 ? 96 : 88) : (kSub == 2 ? 184 : 240);
+  static constexpr int kRegsEpilogue = kCS == 2 ? (D == 128 ? 56 : 64) : (kSub == 2 ? 80 : 128);
+  static constexpr int kRegsOther = kCS == 2 ? (D == 128 ? 40 : 48) : (kSub == 2 ? 56 : 136);
   static constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
   static_assert(128 * (kSub * kCS * kRegsSoftmax + kRegsEpilogue + kRegsOther) <= kThreads * kLaunchRegs,
                 "setmaxnreg split exceeds the launch register allocation");
-  static_assert(kCS == 1 || kPInTmem, "split softmax columns need P in TMEM");
+  static_assert(kCS == 1 || kPInTmem || kRowSplit, "split softmax columns need P in TMEM");
   static_assert(kTmemO + kSub * D <= 512, "TMEM plan overflows 512 columns");
   static_assert(!kPInTmem || kTmemP + kSub * 64 <= kTmemO || kTmemP >= kTmemO + kSub * D,
                 "P columns overlap O");
@@ -160,9 +172,9 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr, uint32_t lb
 // kItemRing slots in shared memory.
 constexpr int kItemRing = 4;
 
-template <int D>
+template <int D, bool WIN = false>
 struct SmemPlan {
-  using C = Cfg<D>;
+  using C = Cfg<D, WIN>;
   static constexpr int kChunkBytes = kBlockM * 128;
   static constexpr int kQTileBytes = kBlockM * D * 2;                 // one sub-tile
   static constexpr int kStageBytes = kBlockN * C::kStageCols * 2;
@@ -190,11 +202,11 @@ struct SmemPlan {
   static constexpr int kItemFull = kMaxX + S * C::kCS;  // [kItemRing]
   static constexpr int kItemEmpty = kItemFull + kItemRing;  // [kItemRing]
   static constexpr int kNumBars = kItemEmpty + kItemRing;
-  // float l[S * kCS][128] (partial row sums), m[S][128]; then (kCS = 2) the row-max
-  // exchange float x[S][kCS][2 tiles][128].
+  // float l[S * kLSlots][128] (row sums, or partial sums of the key halves), m[S][128];
+  // then, for the key-column split, the row-max exchange float x[S][kCS][2 tiles][128].
   static constexpr int kRowStats = (kBars + kNumBars * 8 + 15) / 16 * 16;
-  static constexpr int kXch = kRowStats + (C::kCS + 1) * S * kBlockM * 4;
-  static constexpr int kItems = kXch + (C::kCS == 2 ? S * 2 * 2 * kBlockM * 4 : 0);  // int item[kItemRing]
+  static constexpr int kXch = kRowStats + (C::kLSlots + 1) * S * kBlockM * 4;
+  static constexpr int kItems = kXch + (C::kCS == 2 && !C::kRowSplit ? S * 2 * 2 * kBlockM * 4 : 0);  // int item[kItemRing]
   static constexpr int kMisc = kItems + kItemRing * 4;                      // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kMaxDynamic = 232448;  // 227 KB per CTA on sm_100
@@ -407,12 +419,12 @@ struct ItemReader {
 // WIN: the launch uses a causal sliding window (p.window >= 0); without it the window
 // logic compiles away. VAR: packed variable-length batch (p.cu_seqlens).
 template <int D, typename T, int EMU8, bool WIN, bool VAR>
-__global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
+__global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  using C = Cfg<D>;
-  using Plan = SmemPlan<D>;
+  using C = Cfg<D, WIN>;
+  using Plan = SmemPlan<D, WIN>;
   constexpr int SUB = C::kSub;
   constexpr int NS = C::kNS;
   constexpr int KP = C::kParts;
@@ -435,8 +447,8 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
   constexpr int kWarpProd = kWarpMma + SUB;
 
   auto bar = [&](int slot) -> uint32_t { return sbase + Plan::kBars + slot * 8; };
-  float* row_l = reinterpret_cast<float*>(smem + Plan::kRowStats);   // [SUB * CS][128]
-  float* row_m = row_l + SUB * CS * kBlockM;                          // [SUB][128]
+  float* row_l = reinterpret_cast<float*>(smem + Plan::kRowStats);   // [SUB * kLSlots][128]
+  float* row_m = row_l + SUB * C::kLSlots * kBlockM;                  // [SUB][128]
   int* items = reinterpret_cast<int*>(smem + Plan::kItems);           // [kItemRing]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Plan::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Plan::kMisc + 4);
@@ -488,7 +500,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
   if (warp < kWarpEpi) {
     // =========================================================== softmax ===
     ptx::setmaxnreg_inc<C::kRegsSoftmax>();
-    if constexpr (CS == 2 && !WIN) {
+    if constexpr (C::kRowSplit) {
       // Two warpgroups per sub-tile split its rows: in each 32-lane TMEM quarter, the warp
       // of warpgroup h takes lanes 16h .. 16h + 15 (16-lane tcgen05.ld/st shapes), all 128
       // keys of the tile. Thread t holds rows ra = lb + t/4 and ra + 8, keys 8e + kq + {0,1}
@@ -497,7 +509,7 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       // C2 and the fp16 MLS d=64 shape +4.5 % over splitting the keys with a per-tile row-max
       // exchange (measured alternating builds). Windowed launches keep the key split below:
       // the per-row window bounds push this form past its 88-register budget (spills,
-      // -14 %).
+      // -14 %). P goes to TMEM, or at d = 128 to the sub-tile's shared-memory P buffer.
       const int i = (warp >> 2) >> 1;                     // sub-tile
       const int lb = (warp & 3) * 32 + ((warp >> 2) & 1) * 16;  // first TMEM lane (= row) of this warp
       const int ra = lb + (lane >> 2);
@@ -506,7 +518,10 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
       const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128);
       const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
       const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64);
-      static_assert(D == 64, "the row-split softmax rescales O in one 64-column block");
+      // P in shared memory (d = 128): the SW128 K-major tile of the sub-tile, keys 0-63 and
+      // 64-127 in two 16 KB chunks; 16-byte unit u of row R sits at unit position
+      // u ^ (R & 7). This thread writes the 4-byte word (lane % 4) of its units.
+      const uint32_t sP = sbase + Plan::kP + i * Plan::kPTileBytes + (uint32_t)(lane & 3) * 4;
       const float c = p.scale_log2;
       const float2 c2 = make_float2(c, c);
       uint32_t s_par = 0, le_par = 1, pf_par = 0;
@@ -613,20 +628,37 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
           ptx::tc_fence_after();
           if (__any_sync(0xffffffffu, resc)) {
             // O is quiescent: the previous P.V completed (above) and the next waits for P.
-            uint32_t o[32];
-            ptx::tmem_ld_16x256b_x8(tO, o);
-            ptx::tmem_wait_ld();
-            ptx::reg_fence32(o);
+#pragma unroll 1
+            for (int ch = 0; ch < D / 64; ++ch) {
+              uint32_t o[32];
+              ptx::tmem_ld_16x256b_x8(tO + ch * 64, o);
+              ptx::tmem_wait_ld();
+              ptx::reg_fence32(o);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              o[4 * e] = __float_as_uint(__uint_as_float(o[4 * e]) * alpha[0]);
-              o[4 * e + 1] = __float_as_uint(__uint_as_float(o[4 * e + 1]) * alpha[0]);
-              o[4 * e + 2] = __float_as_uint(__uint_as_float(o[4 * e + 2]) * alpha[1]);
-              o[4 * e + 3] = __float_as_uint(__uint_as_float(o[4 * e + 3]) * alpha[1]);
+              for (int e = 0; e < 8; ++e) {
+                o[4 * e] = __float_as_uint(__uint_as_float(o[4 * e]) * alpha[0]);
+                o[4 * e + 1] = __float_as_uint(__uint_as_float(o[4 * e + 1]) * alpha[0]);
+                o[4 * e + 2] = __float_as_uint(__uint_as_float(o[4 * e + 2]) * alpha[1]);
+                o[4 * e + 3] = __float_as_uint(__uint_as_float(o[4 * e + 3]) * alpha[1]);
+              }
+              ptx::tmem_st_16x256b_x8(tO + ch * 64, o);
             }
-            ptx::tmem_st_16x256b_x8(tO, o);
           }
-          ptx::tmem_st_16x128b_x16(tP, pk);
+          if constexpr (C::kPInTmem) {
+            ptx::tmem_st_16x128b_x16(tP, pk);
+          } else {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+              const int row = ra + 8 * rr;
+              const uint32_t rowp = sP + (uint32_t)row * 128;
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                ptx::st_shared_b32(rowp + (uint32_t)(e >> 3) * Plan::kChunkBytes +
+                                       (((uint32_t)(e & 7) ^ (uint32_t)(row & 7)) << 4),
+                                   pk[2 * e + rr]);
+            }
+            ptx::fence_proxy_async_smem();
+          }
           ptx::tmem_wait_st();
           ptx::tc_fence_before();
           ptx::mbar_arrive(bar(Plan::kPFull + i));
@@ -640,11 +672,9 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
         if (!(ok = W.wait_warp(bar(Plan::kLEmpty + i), le_par))) break;
         le_par ^= 1;
         if ((lane & 3) == 0) {
-          // Full row sums in the first slot; the epilogue adds both slots.
 #pragma unroll
           for (int rr = 0; rr < 2; ++rr) {
-            row_l[(i * CS) * kBlockM + ra + 8 * rr] = l[rr];
-            row_l[(i * CS + 1) * kBlockM + ra + 8 * rr] = 0.f;
+            row_l[i * kBlockM + ra + 8 * rr] = l[rr];  // one slot per sub-tile: the full row sum
             row_m[i * kBlockM + ra + 8 * rr] = m[rr];
           }
         }
@@ -828,8 +858,8 @@ __global__ void __launch_bounds__(Cfg<D>::kThreads, 1)
     auto finish = [&](const WorkItem& it, const int i) -> bool {
       if (!W.wait_warp(bar(Plan::kLFull + i), (lf_par >> i) & 1u)) return false;
       lf_par ^= 1u << i;
-      float l = row_l[(i * CS) * kBlockM + r];
-      if (CS == 2) l += row_l[(i * CS + 1) * kBlockM + r];
+      float l = row_l[(i * C::kLSlots) * kBlockM + r];
+      if (C::kLSlots == 2) l += row_l[(i * C::kLSlots + 1) * kBlockM + r];
       const float m = row_m[i * kBlockM + r];
       ptx::mbar_arrive(bar(Plan::kLEmpty + i));
       if (!W.wait_warp(bar(Plan::kOFull + i), (of_par >> i) & 1u)) return false;
