@@ -274,7 +274,7 @@ def custom_attention_varlen_backward(q, k, v, o, lse, dout, cu_seqlens, max_seql
     return dq, dk, dv
 
 
-_FWD_KERNELS = {"auto": 0, "two_subtile": 1, "tile": 2, "pair": 3}
+_FWD_KERNELS = {"auto": 0, "two_subtile": 1, "tile": 2}
 
 
 def set_forward_kernel(kind: str = "auto") -> None:
@@ -282,8 +282,7 @@ def set_forward_kernel(kind: str = "auto") -> None:
     batched head dims 64 and 128 without a window, the kernel with the shorter estimated
     makespan, which is the tile kernel only for problems too small to fill the GPU with
     256-row items; the two-sub-tile kernel otherwise), "two_subtile" (that kernel
-    everywhere), "tile" (the tile kernel wherever it applies) or "pair" (the CTA-pair
-    kernel wherever it applies: batched, head dim 128, no window). All give results within
+    everywhere) or "tile" (the tile kernel wherever it applies). Both give results within
     the operator's tolerance; this exists to measure them side by side."""
     if kind not in _FWD_KERNELS:
         raise ValueError(f"kind must be one of {sorted(_FWD_KERNELS)}, got {kind!r}")

@@ -23,7 +23,6 @@
 #include "apex_attn.h"
 #include "attn_bwd_kernel.cuh"
 #include "attn_fwd_kernel.cuh"
-#include "attn_fwd_pair_kernel.cuh"
 #include "attn_fwd_tile_kernel.cuh"
 
 namespace {
@@ -61,8 +60,7 @@ template <int D>
 constexpr int kEmuTile = D == 64 ? APEX_TILE_EMU64 : APEX_TILE_EMU128;
 
 // Forward kernel selection (apex_attn_set_forward_kernel): 0 = automatic, 1 = the
-// two-sub-tile kernel for every call, 2 = the tile kernel wherever it applies, 3 = the
-// CTA-pair kernel wherever it applies.
+// two-sub-tile kernel for every call, 2 = the tile kernel wherever it applies.
 std::atomic<int> g_fwd_kind{0};
 
 constexpr int kMaxDevices = 64;
@@ -244,13 +242,13 @@ int device_of(const void* ptr) {
 // 4-D tiled map over a logical [B, H, N, D] tensor, dims ordered (D, N, H, B), box
 // (64, 128, 1, 1), 128-byte swizzle, zero fill out of bounds (rows >= N read as 0).
 int encode_map(CUtensorMap* m, const void* ptr, int dtype, int B, int H, int N, int D, long long sb,
-               long long sh, long long sn, int box_rows = apex::kBlockM) {
+               long long sh, long long sn) {
   // Strides of size-1 dims are never used; give them a legal value.
   if (H == 1) sh = (long long)N * sn;
   if (B == 1) sb = (long long)H * sh;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)sn * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
-  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)apex::kBlockM, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = g_encode(m, dtype == APEX_ATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                         4, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -334,31 +332,8 @@ __global__ void wait_timeout_selftest_kernel(int* status, int* host_flag, unsign
 bool supported_head_dim(int head_dim) { return head_dim == 64 || head_dim == 128 || head_dim == 256; }
 
 int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUtensorMap& mq,
-                        const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap* mo,
-                        const CUtensorMap* mk64, int head_dim, int dtype, void* stream);
-
-template <typename T>
-int launch_pair(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk64,
-                const CUtensorMap& mv, const AttnParams& p, int grid, cudaStream_t stream) {
-  auto kern = apex::attn_fwd_pair_kernel<T, kEmu<128>>;
-  constexpr int smem = apex::PairPlan::kDynamicBytes;
-  if (!(ds.attr_tile & attr_bit)) {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return APEX_ATTN_ERR_LAUNCH;
-    }
-    ds.attr_tile |= attr_bit;
-  }
-  kern<<<grid, apex::PairCfg::kThreads, smem, stream>>>(mq, mk64, mv, p);  // clusters of 2 (kernel attribute)
-  if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
-  return APEX_ATTN_OK;
-}
-
-// The CTA-pair kernel covers batched launches at head dim 128 without a window.
-bool use_pair_kernel(int head_dim, int window) {
-  return g_fwd_kind.load(std::memory_order_relaxed) == 3 && head_dim == 128 && window < 0;
-}
+                        const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap* mo, int head_dim,
+                        int dtype, void* stream);
 
 template <int D, typename T>
 int launch_tile(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const CUtensorMap& mk,
@@ -391,7 +366,7 @@ int launch_tile(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const
 //     and loses up to 14 %, so automatic selection keeps the two-sub-tile kernel.
 bool use_tile_kernel(int head_dim, const AttnParams& p, const CUtensorMap* mo, int num_sms) {
   const int kind = g_fwd_kind.load(std::memory_order_relaxed);
-  if (kind == 1 || kind == 3 || mo == nullptr || (head_dim != 64 && head_dim != 128) || p.window >= 0 ||
+  if (kind == 1 || mo == nullptr || (head_dim != 64 && head_dim != 128) || p.window >= 0 ||
       p.cu_seqlens != nullptr)
     return false;
   if (kind == 2) return true;
@@ -452,24 +427,18 @@ int forward(bool noalloc, const void* q, const void* k, const void* v, void* o, 
   p.window = window < seqlen ? window : -1;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
-  CUtensorMap mk64;  // K in 64-row boxes: each CTA of a pair loads half of a K tile
-  const bool pair = use_pair_kernel(head_dim, p.window);
-  if (pair && (rc = encode_map(&mk64, k, dtype, batch, heads_kv, seqlen, head_dim, strides[3], strides[4],
-                               strides[5], 64)))
-    return rc;
-  return schedule_and_launch(*ds, noalloc, p, mq, mk, mv, &mo, pair ? &mk64 : nullptr, head_dim, dtype, stream);
+  return schedule_and_launch(*ds, noalloc, p, mq, mk, mv, &mo, head_dim, dtype, stream);
 }
 
 // Scheduling parameters, scratch, and the launch shared by every forward entry point. The
 // caller filled the output, shape, mask and scale fields of p.
 int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUtensorMap& mq,
-                        const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap* mo,
-                        const CUtensorMap* mk64, int head_dim, int dtype, void* stream) {
+                        const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap* mo, int head_dim,
+                        int dtype, void* stream) {
   DeviceState* ds = &dst;
   const long long BH = (long long)p.B * p.H;
-  const bool pair = mk64 != nullptr;
-  const bool tile = !pair && use_tile_kernel(head_dim, p, mo, ds->num_sms);
-  const int rows_per_item = pair ? apex::PairCfg::kItemRows : (tile ? apex::kBlockM : item_rows(head_dim));
+  const bool tile = use_tile_kernel(head_dim, p, mo, ds->num_sms);
+  const int rows_per_item = tile ? apex::kBlockM : item_rows(head_dim);
   const long long mblocks = (p.N + rows_per_item - 1) / rows_per_item;
   p.status = ds->status;
   p.host_flag = ds->host_flag_dev;
@@ -533,11 +502,6 @@ int schedule_and_launch(DeviceState& dst, bool noalloc, AttnParams& p, const CUt
     return APEX_ATTN_ERR_CUDA;
   }
   const bool bf16 = dtype == APEX_ATTN_BF16;
-  if (pair) {
-    const int clusters = std::min(p.num_items, std::max(1, ds->num_sms / 2));
-    return bf16 ? launch_pair<__nv_bfloat16>(*ds, 1u << 8, mq, *mk64, mv, p, 2 * clusters, s)
-                : launch_pair<__half>(*ds, 1u << 9, mq, *mk64, mv, p, 2 * clusters, s);
-  }
   if (tile) {
     if (head_dim == 64)
       return bf16 ? launch_tile<64, __nv_bfloat16>(*ds, 1u, mq, mk, mv, *mo, p, grid, s)
@@ -614,7 +578,7 @@ int forward_varlen(const apex_attn_varlen_args* a, void* stream) {
   p.scale_log2 = a->sm_scale * 1.4426950408889634f;
   p.cu_seqlens = a->cu_seqlens;
   p.total = a->total;
-  return schedule_and_launch(*ds, false, p, mq, mk, mv, nullptr, nullptr, a->head_dim, a->dtype, stream);
+  return schedule_and_launch(*ds, false, p, mq, mk, mv, nullptr, a->head_dim, a->dtype, stream);
 }
 
 // ------------------------------------------------------------------ backward --
@@ -968,7 +932,7 @@ int apex_attn_noalloc_status(int device, int* flags) {
 }
 
 int apex_attn_set_forward_kernel(int kind) {
-  if (kind < 0 || kind > 3) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (kind < 0 || kind > 2) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   g_fwd_kind.store(kind, std::memory_order_relaxed);
   return APEX_ATTN_OK;
 }

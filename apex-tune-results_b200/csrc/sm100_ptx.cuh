@@ -365,109 +365,5 @@ __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
-// ---------------------------------------------------------- CTA pairs -------
-// Forms for a cluster of two CTAs whose tensor-core work is issued by the first (rank 0)
-// as cta_group::2 instructions: M = 256 MMAs whose A rows and B columns are split between
-// the two CTAs' shared memories and whose accumulator rows land in both CTAs' TMEM.
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Address, in the shared::cluster window, of `cta_addr` (a shared::cta address) in the
-// shared memory of cluster CTA `rank`.
-__device__ __forceinline__ uint32_t mapa(uint32_t cta_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(cta_addr), "r"(rank));
-  return r;
-}
-
-// Arrive on an mbarrier in any CTA of the cluster (release at cluster scope).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-// Arrive on an mbarrier in any CTA of the cluster, with release at CTA scope: for signals
-// that carry no shared-memory data for the other CTA's threads (TMEM reads done, or
-// operands that this CTA's own tensor core reads after this thread's proxy fence). A
-// cluster-scope release costs ~1,000 cycles per arrival on B200 (measured).
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-// try_wait with cluster-scope acquire: for barriers that other CTAs of the cluster arrive on.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
-}
-
-// All threads of both CTAs: arrive, then wait (release/acquire at cluster scope).
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// Pair MMA, D[tmem] (+)= A[smem desc] * B[smem desc], issued by one elected lane of a
-// converged warp of rank 0. Each CTA supplies the A rows and B columns at the same
-// shared-memory offsets.
-__device__ __forceinline__ void umma_ss_pair_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                                  uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "elect.sync _|q, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@q tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive once on the mbarrier at `bar` (a shared::cta offset) in each CTA of `cta_mask`
-// when every pair MMA this thread issued so far has completed; one elected lane.
-__device__ __forceinline__ void tc_commit_pair_warp(uint32_t bar, uint16_t cta_mask) {
-  asm volatile(
-      "{\n\t.reg .pred q;\n\t"
-      "elect.sync _|q, 0xffffffff;\n\t"
-      "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(bar),
-      "h"(cta_mask)
-      : "memory");
-}
-
-// Tiled 4-D tensor load into this CTA's shared memory for pair MMAs; its completion is
-// signalled on the mbarrier at `cluster_bar` (shared::cluster window), which may be the
-// other CTA's. No multicast: each CTA loads only its own part.
-__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* tmap, uint32_t cluster_bar, int x, int y,
-                                                 int z, int w, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
-      : "memory");
-}
-
 }  // namespace ptx
 }  // namespace apex

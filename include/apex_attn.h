@@ -148,11 +148,8 @@ int apex_attn_fwd_varlen(const apex_attn_varlen_args* args, void* stream);
  *      TMA-store epilogue) for problems too small to fill the GPU with 256-row items,
  *      else the two-sub-tile kernel; the two-sub-tile kernel for every other call;
  *   1  the two-sub-tile kernel for every call;
- *   2  the tile kernel wherever it applies (batched, head dim 64 or 128, no window);
- *   3  the CTA-pair kernel wherever it applies (batched, head dim 128, no window): clusters
- *      of two CTAs whose M = 256 tensor-core instructions each read half of every K and V
- *      tile from each CTA.
- * All kernels compute the same function within the stated tolerances; this exists to
+ *   2  the tile kernel wherever it applies (batched, head dim 64 or 128, no window).
+ * Both kernels compute the same function within the stated tolerances; this exists to
  * measure them against each other. Returns APEX_ATTN_ERR_INVALID_ARGUMENT for other values.
  * No counterpart in the reference (its _CONFIGS table picks one kernel per head dim,
  * fused_attention.py:148-152).
