@@ -98,6 +98,12 @@ SYMBOLS = {
                                      ctypes.c_void_p]),
     "apex_attn_bwd_varlen": (ctypes.c_int, [ctypes.POINTER(BwdVarlenArgs), ctypes.c_void_p,
                                             ctypes.c_size_t, ctypes.c_void_p]),
+    "apex_attn_bwd_workspace_bytes_mode": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                             ctypes.c_int, ctypes.c_int]),
+    "apex_attn_bwd_mode": (ctypes.c_int, [ctypes.POINTER(BwdArgs), ctypes.c_int, ctypes.c_void_p,
+                                          ctypes.c_size_t, ctypes.c_void_p]),
+    "apex_attn_bwd_varlen_mode": (ctypes.c_int, [ctypes.POINTER(BwdVarlenArgs), ctypes.c_int,
+                                                 ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "apex_attn_num_sms_hint": (ctypes.c_int, [ctypes.c_int]),
     "apex_attn_set_forward_kernel": (ctypes.c_int, [ctypes.c_int]),
     "apex_attn_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),

@@ -155,7 +155,11 @@ def custom_attention_varlen_forward(q, k, v, cu_seqlens, max_seqlen, causal=True
     return (o, lse) if return_lse else o
 
 
-def custom_attention_backward(q, k, v, o, lse, dout, causal=True, sm_scale=None, window_left=None):
+_BWD_MODES = {True: 0, False: 1}  # APEX_ATTN_BWD_DETERMINISTIC, APEX_ATTN_BWD_FUSED
+
+
+def custom_attention_backward(q, k, v, o, lse, dout, causal=True, sm_scale=None, window_left=None,
+                              deterministic=True):
     """Gradients (dq, dk, dv) of custom_attention_forward for the upstream gradient `dout`.
 
     The backward nanochat's attention op calls (``_flash_attn_bwd(q, k, v, out,
@@ -164,7 +168,12 @@ def custom_attention_backward(q, k, v, o, lse, dout, causal=True, sm_scale=None,
     output and fp32 logsumexp (``custom_attention_forward(..., return_lse=True)``); the
     other arguments mean what they mean for the forward. Head dims 64 and 128 (others
     raise KeyError). dq has q's shape, dk and dv k's (grouped-query heads summed); all in
-    q's dtype. Runs asynchronously on the current CUDA stream; deterministic.
+    q's dtype. Runs asynchronously on the current CUDA stream.
+
+    deterministic=True (default): two passes, bitwise reproducible. False: the fused
+    one-pass algorithm, faster, whose dq is accumulated in fp32 with global reductions and
+    so varies in its last bits from run to run (dk, dv do not); it needs a workspace of
+    4 * B * H * N * D more bytes.
     """
     if q.dim() != 4 or k.shape != v.shape or o.shape != q.shape or dout.shape != q.shape:
         raise ValueError(f"expected q, o, dout [B, H, N, D] and k, v [B, H_kv, N, D], got q "
@@ -196,7 +205,8 @@ def custom_attention_backward(q, k, v, o, lse, dout, causal=True, sm_scale=None,
     if q.numel() == 0:
         return dq, dk.zero_(), dv.zero_()
     lib = _lib.load()
-    ws_bytes = int(lib.apex_attn_bwd_workspace_bytes(batch, nheads, seqlen))
+    mode = _BWD_MODES[bool(deterministic)]
+    ws_bytes = int(lib.apex_attn_bwd_workspace_bytes_mode(batch, nheads, seqlen, headdim, mode))
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     strides = []
     for t in (q, k, v, o, dout, dq, dk, dv):
@@ -209,17 +219,18 @@ def custom_attention_backward(q, k, v, o, lse, dout, causal=True, sm_scale=None,
                         window_left=-1 if window_left is None else int(window_left),
                         sm_scale=float(sm_scale), strides=(ctypes.c_longlong * 24)(*strides))
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    rc = lib.apex_attn_bwd(ctypes.byref(args), workspace.data_ptr(), ws_bytes, stream)
+    rc = lib.apex_attn_bwd_mode(ctypes.byref(args), mode, workspace.data_ptr(), ws_bytes, stream)
     _lib.check(rc, "custom_attention_backward")
     return dq, dk, dv
 
 
 def custom_attention_varlen_backward(q, k, v, o, lse, dout, cu_seqlens, max_seqlen, causal=True,
-                                     sm_scale=None, window_left=None):
+                                     sm_scale=None, window_left=None, deterministic=True):
     """Gradients (dq, dk, dv) of custom_attention_varlen_forward: packed q, o, dout
     [total, H, D], k, v [total, H_kv, D], lse fp32 [H, total] from the forward, cu_seqlens and
     max_seqlen as for the forward. Head dims 64 and 128. Rows outside every sequence come
-    back as zeros. Deterministic; asynchronous on the current stream.
+    back as zeros. Asynchronous on the current stream; `deterministic` as for
+    custom_attention_backward.
     """
     if q.dim() != 3 or k.shape != v.shape or o.shape != q.shape or dout.shape != q.shape:
         raise ValueError("expected q, o, dout [total, H, D] and k, v [total, H_kv, D]")
@@ -255,7 +266,8 @@ def custom_attention_varlen_backward(q, k, v, o, lse, dout, cu_seqlens, max_seql
         return dq, dk, dv
     batch = cu_seqlens.numel() - 1
     lib = _lib.load()
-    ws_bytes = int(lib.apex_attn_bwd_workspace_bytes(batch, nheads, int(max_seqlen)))
+    mode = _BWD_MODES[bool(deterministic)]
+    ws_bytes = int(lib.apex_attn_bwd_workspace_bytes_mode(batch, nheads, int(max_seqlen), headdim, mode))
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     strides = []
     for t in (q, k, v, o, dout, dq, dk, dv):
@@ -269,7 +281,7 @@ def custom_attention_varlen_backward(q, k, v, o, lse, dout, cu_seqlens, max_seql
                               window_left=-1 if window_left is None else int(window_left),
                               sm_scale=float(sm_scale), strides=(ctypes.c_longlong * 16)(*strides))
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    rc = lib.apex_attn_bwd_varlen(ctypes.byref(args), workspace.data_ptr(), ws_bytes, stream)
+    rc = lib.apex_attn_bwd_varlen_mode(ctypes.byref(args), mode, workspace.data_ptr(), ws_bytes, stream)
     _lib.check(rc, "custom_attention_varlen_backward")
     return dq, dk, dv
 

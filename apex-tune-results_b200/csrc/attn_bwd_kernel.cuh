@@ -25,6 +25,9 @@
 // The dQ pass recomputes S and dP (3 GEMMs per tile) instead of accumulating dQ with
 // atomics from the dK/dV pass, trading 40% more tensor work for deterministic results and
 // no fp32 dQ scratch.
+// The fused mode (DQ = true) instead runs launch 2 with a fifth GEMM per step, dQ = dS K,
+// whose tiles warps 12-15 add into a zeroed fp32 accumulator with global reductions; a
+// cast kernel (attn_bwd_dq_cast_kernel) then writes dq = scale * acc.
 //
 // TMEM and scheduling (both passes, 128 x 128 tiles, one CTA per SM):
 //   T1 [0, 128)     scores S^T | S (fp32). The elementwise warps read them into registers
@@ -86,6 +89,9 @@ struct BwdParams {
   int kv_group;          // H / Hkv
   float scale_log2;      // sm_scale * log2(e)
   float out1_scale;      // sm_scale (dK = scale dS^T Q, dQ = scale dS K)
+  // Fused form: fp32 dQ accumulator, zeroed before the launch; [B][H][N][D], or [H][total][D]
+  // for a packed batch. Unscaled: it holds dS K, and the cast to the output applies scale.
+  float* dq_acc;
   int causal;
   int window;            // -1: none
   // Packed variable-length batch (VAR kernels): sequence b is rows
@@ -97,23 +103,29 @@ struct BwdParams {
   unsigned long long timeout_ns;
 };
 
-template <int D>
+// DQ: the fused one-pass form of the dK/dV pass (see attn_bwd_sm100_kernel).
+template <int D, bool DQ = false>
 struct BwdCfg {
   static_assert(D == 64 || D == 128, "backward head dims 64, 128");
   // Streaming ring stages (one 128-row tile each). A stage frees when the accumulating GEMMs
   // of its step finish and takes ~1300 cycles to refill from L2, so the ring holds about
-  // two and a half steps (two tiles per step).
-  static constexpr int kNS = D == 64 ? 10 : 5;
-  // 12 warps: 8 elementwise, MMA, producer, 2 idle. Registers are granted per warpgroup,
-  // so the launch budget is 384 x 168; setmaxnreg moves it to the elementwise warpgroups
-  // (the split must not exceed the launch allocation, or setmaxnreg.inc would never return).
-  static constexpr int kThreads = 384;
+  // two and a half steps (two tiles per step). The fused form gives 64 KB to the dS tile
+  // and the dQ staging chunks.
+  static constexpr int kNS = DQ ? (D == 64 ? 8 : 3) : (D == 64 ? 10 : 5);
+  // 12 warps: 8 elementwise, MMA, producer, 2 idle (+ 4 dQ warps in the fused form).
+  // Registers are granted per warpgroup, so the launch budget is kThreads x (65536 /
+  // kThreads); setmaxnreg moves it to the elementwise warpgroups (the split must not exceed
+  // the launch allocation, or setmaxnreg.inc would never return).
+  static constexpr int kThreads = DQ ? 512 : 384;
   static constexpr int kWarpMma = 8;
   static constexpr int kWarpProd = 9;
-  static constexpr int kRegsElementwise = 224;
-  static constexpr int kRegsOther = 56;
+  static constexpr int kWarpDq = 12;  // fused form: warps 12-15 reduce dQ tiles into global memory
+  // Fused splits: the ones without spills in the plain (unwindowed, batched) builds.
+  static constexpr int kRegsElementwise = DQ ? 200 : 224;
+  static constexpr int kRegsOther = DQ && D == 64 ? 48 : 56;
+  static constexpr int kRegsDq = DQ ? (D == 64 ? 64 : 56) : 0;
   static constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
-  static_assert(128 * (2 * kRegsElementwise + kRegsOther) <= kThreads * kLaunchRegs,
+  static_assert(128 * (2 * kRegsElementwise + kRegsOther + kRegsDq) <= kThreads * kLaunchRegs,
                 "setmaxnreg split exceeds the launch register allocation");
   // TMEM columns: T1 scores, T2 dP (then packed P / dS), Acc1 dK | dQ, Acc2 dV (KV pass),
   // XQ / XdO the item's Q and dO as 16-bit pairs (Q pass).
@@ -123,21 +135,40 @@ struct BwdCfg {
   static constexpr int kAcc2 = 256 + D;
   static constexpr int kXQ = 256 + D;
   static constexpr int kXdO = kXQ + D / 2;
+  // Fused form: the step's dQ tile (fp32, 128 query rows x D). At d = 64 two buffers fit
+  // behind dV. At d = 128 TMEM is full: dQ borrows T2 once the step's dV and dK GEMMs have
+  // read P and dS from it, and the next dP GEMM writes each 64-column half of T2 once the
+  // dQ warps have read that half out. T1 stays free for the next score GEMM, which keeps
+  // running during the elementwise work.
+  static constexpr int kDqBufs = D == 64 ? 2 : 1;
+  static constexpr int kDq = D == 64 ? 256 + 2 * D : kT2;
+  static constexpr bool kDqInT2 = DQ && D == 128;
+  static constexpr int kDqStage = 2;  // 16 KB shared-memory staging chunks (128 rows x 32 fp32);
+                                      // the dQ warps' bulk_wait_group_read1 assumes 2
   static_assert(kAcc2 + D <= 512 && kXdO + D / 2 <= 512, "TMEM plan overflows 512 columns");
+  static_assert(!DQ || kDqInT2 || kDq + kDqBufs * D <= 512, "dQ buffers overflow TMEM");
 };
 
-template <int D>
+template <int D, bool DQ = false>
 struct BwdSmem {
-  using C = BwdCfg<D>;
+  using C = BwdCfg<D, DQ>;
   static constexpr int NS = C::kNS;
   static constexpr int kChunkBytes = kBlockM * 128;
   static constexpr int kTileBytes = kBlockM * D * 2;
   static constexpr int kX1 = 0;
   static constexpr int kX2 = kX1 + kTileBytes;
   static constexpr int kRing = kX2 + kTileBytes;
+  // Fused form: dS^T of the step, 128 key rows x 128 query columns (16-bit) in two SW128
+  // chunks of 64 queries; the dQ GEMM reads it as an MN-major A operand (dS).
+  static constexpr int kDs = kRing + NS * kTileBytes;
+  static constexpr int kDsBytes = DQ ? 2 * kChunkBytes : 0;
+  // Fused form: staging chunks of the dQ tile for the TMA reduce, each 128 rows x 32 fp32
+  // (128 bytes per row, 128-byte swizzle: the box layout of the accumulator's tensor map).
+  static constexpr int kStage = kDs + kDsBytes;
+  static constexpr int kStageBytes = DQ ? C::kDqStage * kChunkBytes : 0;
   // KV pass: per-column statistics of the step's query tile, double-buffered:
   // float [2][256] = -lse2[128], -delta[128].
-  static constexpr int kStats = kRing + NS * kTileBytes;
+  static constexpr int kStats = kStage + kStageBytes;
   static constexpr int kStatsBytes = 1024;
   static constexpr int kBars = kStats + 2 * kStatsBytes;
   static constexpr int kRingFull = 0;
@@ -156,7 +187,10 @@ struct BwdSmem {
   static constexpr int kAccFull = kStatsEmpty + 2;
   static constexpr int kAccEmpty = kAccFull + 1;
   static constexpr int kDrain = kAccEmpty + 1;
-  static constexpr int kItemFull = kDrain + 1;
+  static constexpr int kDqFull = kDrain + 1;    // [2] fused form: dQ tile in TMEM buffer b
+  // [2] fused form: dQ buffer b read out (d = 128: 64-column half b of the one buffer)
+  static constexpr int kDqFree = kDqFull + 2;
+  static constexpr int kItemFull = kDqFree + 2;
   static constexpr int kItemEmpty = kItemFull + kItemRing;
   static constexpr int kNumBars = kItemEmpty + kItemRing;
   static constexpr int kItems = kBars + kNumBars * 8;
@@ -167,6 +201,7 @@ struct BwdSmem {
   // memory base being 1 KB aligned and checks it (as the forward does).
   static constexpr int kDynamicBytes = kBytes + 1024 <= kMaxDynamic ? kBytes + 1024 : kBytes;
   static_assert(kBytes <= kMaxDynamic, "shared-memory plan exceeds 227 KB");
+  static_assert(kDs % 1024 == 0, "SW128 tiles need 1 KB alignment");
 };
 
 // One work item: the stationary 128-row block `blk` of head `hx` (K/V head in the KV pass,
@@ -284,16 +319,65 @@ __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const T* __restrict_
   }
 }
 
+// Fused backward, last launch: dq = scale * acc in the output dtype, for the rows the
+// two-pass form writes: row i < len of every (batch, head). Rows are walked as in the prep
+// kernel, [B * H][Npad]; acc is fp32 [B][H][N][D], or [H][total][D] for a packed batch
+// (sequence b at token cu_seqlens[b], clamped as in the attention kernels). kTpr = D / 8
+// threads per row, each converting 8 elements.
+template <typename T, int D, bool VAR>
+__global__ void __launch_bounds__(256) attn_bwd_dq_cast_kernel(const float* __restrict__ acc, T* __restrict__ dq,
+                                                               long long sb, long long sh, long long sn, int H,
+                                                               int N, int Npad, long long rows,
+                                                               const int* cu_seqlens, int total, float scale) {
+  constexpr int kTpr = D / 8;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long row = idx / kTpr;
+  if (row >= rows) return;
+  const int sub = (int)(idx % kTpr);
+  const int i = (int)(row % Npad);
+  const long long bh = row / Npad;
+  const int b = (int)(bh / H);
+  const int h = (int)(bh - (long long)b * H);
+  long long arow, orow;  // accumulator row, and element offset of the output row
+  if (VAR) {
+    const int a0 = min(max(__ldg(cu_seqlens + b), 0), total);
+    const int e0 = min(max(__ldg(cu_seqlens + b + 1), a0), total);
+    if (i >= min(e0 - a0, N)) return;
+    arow = (long long)h * total + a0 + i;
+    orow = (long long)h * sh + (long long)(a0 + i) * sn;
+  } else {
+    if (i >= N) return;
+    arow = bh * N + i;
+    orow = (long long)b * sb + (long long)h * sh + (long long)i * sn;
+  }
+  const float4* src = reinterpret_cast<const float4*>(acc + arow * D + sub * 8);
+  const float4 x = src[0], y = src[1];
+  uint4 o;
+  o.x = DType<T>::pack(x.x * scale, x.y * scale);
+  o.y = DType<T>::pack(x.z * scale, x.w * scale);
+  o.z = DType<T>::pack(y.x * scale, y.y * scale);
+  o.w = DType<T>::pack(y.z * scale, y.w * scale);
+  *reinterpret_cast<uint4*>(dq + orow + sub * 8) = o;
+}
+
 // KV = true: dK, dV pass; KV = false: dQ pass. WIN: causal sliding window in use. VAR:
-// packed variable-length batch.
-template <int D, typename T, bool KV, bool WIN, bool VAR>
-__global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
+// packed variable-length batch. DQ (with KV): the fused one-pass backward. Each step also
+// writes dS^T to shared memory and computes the step's dQ tile, dQ(query tile) = dS K
+// (A = the dS^T tile read MN-major, B = the item's K read MN-major), into TMEM; warps 12-15
+// read it out through shared-memory staging chunks and add it into the fp32 accumulator
+// p.dq_acc with TMA reduce-adds over tmDq (fp32 (D, rows, B * H), or (D, total, H) for a
+// packed batch; box 32 x 128 x 1). Five GEMMs per step instead of the seven of the two
+// passes; dQ sums in whatever order the CTAs reach it, so it is not bitwise reproducible.
+template <int D, typename T, bool KV, bool WIN, bool VAR, bool DQ = false>
+__global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
     attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmX1,
                           const __grid_constant__ CUtensorMap tmX2,
                           const __grid_constant__ CUtensorMap tmY1,
-                          const __grid_constant__ CUtensorMap tmY2, const BwdParams p) {
-  using C = BwdCfg<D>;
-  using Plan = BwdSmem<D>;
+                          const __grid_constant__ CUtensorMap tmY2,
+                          const __grid_constant__ CUtensorMap tmDq, const BwdParams p) {
+  static_assert(!DQ || KV, "the fused form is a variant of the dK/dV pass");
+  using C = BwdCfg<D, DQ>;
+  using Plan = BwdSmem<D, DQ>;
   constexpr int NS = C::kNS;
   constexpr int kEmu = D == 64 ? APEX_BWD_EMU64 : APEX_BWD_EMU128;
   extern __shared__ uint8_t smem_raw[];
@@ -335,10 +419,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     ptx::mbar_init(bar(Plan::kAccFull), 1);
     ptx::mbar_init(bar(Plan::kAccEmpty), 256);
     ptx::mbar_init(bar(Plan::kDrain), 1);
-    // Item-ring readers: the 8 elementwise warps and the MMA warp.
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(bar(Plan::kDqFull + b), 1);
+      ptx::mbar_init(bar(Plan::kDqFree + b), 128);
+    }
+    // Item-ring readers: the 8 elementwise warps, the MMA warp (and the 4 dQ warps).
     for (int k = 0; k < kItemRing; ++k) {
       ptx::mbar_init(bar(Plan::kItemFull + k), 1);
-      ptx::mbar_init(bar(Plan::kItemEmpty + k), 9);
+      ptx::mbar_init(bar(Plan::kItemEmpty + k), DQ ? 13 : 9);
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -352,6 +440,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     ptx::prefetch_tmap(&tmX2);
     ptx::prefetch_tmap(&tmY1);
     ptx::prefetch_tmap(&tmY2);
+    if (DQ) ptx::prefetch_tmap(&tmDq);
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -496,6 +585,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             }
           }
         }
+        // Fused form, packed batch, full attention: keys of this item past the sequence end
+        // (the next sequence's) would add to dQ = dS K, so their rows of P (and so dS) are
+        // zeroed. Their dK, dV rows are never stored. (Batched inputs read zero-filled K
+        // there, and causal masks hide such keys.)
+        if (DQ && VAR && !p.causal && it.blk * kBlockN + r >= it.len) {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) pv[e] = 0.f;
+        }
         uint32_t pk_p[32];
         if (KV) {
 #pragma unroll
@@ -529,6 +626,15 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
               pk_s[(e >> 1) + 1] = DType<T>::pack(a23.x, a23.y);
             }
             ptx::tmem_st32(tT2 + 32, pk_s);  // dS_h after P_h
+            if (DQ) {
+              // The same dS^T row into the shared-memory tile of the dQ GEMM: chunk `half`
+              // (queries 64 half ..), row r, 16-byte unit u at position u ^ (r & 7).
+              const uint32_t drow = sbase + Plan::kDs + half * Plan::kChunkBytes + r * 128;
+#pragma unroll
+              for (int u = 0; u < 8; ++u)
+                ptx::st_shared_v4(drow + (((uint32_t)u ^ (uint32_t)(r & 7)) << 4), pk_s[4 * u], pk_s[4 * u + 1],
+                                  pk_s[4 * u + 2], pk_s[4 * u + 3]);
+            }
             ptx::mbar_arrive(bar(Plan::kStatsEmpty + sslot));  // statistics read
           } else {
             const float2 nd = make_float2(row_ndelta, row_ndelta);
@@ -542,6 +648,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           }
           ptx::tmem_wait_st();
         }
+        if (DQ) ptx::fence_proxy_async_smem();  // the dS tile, for the dQ GEMM
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(Plan::kPdSFull + half));
       }
@@ -590,6 +697,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     constexpr uint32_t idNT = make_idesc<T>(kBlockM, kBlockN, false);  // T1 = X Y^T
     constexpr uint32_t idNT64 = make_idesc<T>(kBlockM, 64, false);     // T2_h = X Y_h^T
     constexpr uint32_t idAcc = make_idesc<T>(kBlockM, D, true);        // Acc += A_h(TMEM) Y_h
+    constexpr uint32_t idDq = make_idesc<T>(kBlockM, D, true, true);   // dQ = dS K, both MN-major
     constexpr uint32_t kHalfRows = 64 * 128;  // byte offset of row 64 inside a 128-row chunk
     // dP as two 64-column GEMMs. Free in the Q pass (A = dO from TMEM, B 2 KB per
     // instruction); in the KV pass both operands come from shared memory and a 64-wide
@@ -620,6 +728,18 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                           (accumulate || kk > 0) ? 1u : 0u);
       }
     };
+    // Fused form: dQ(step) = dS K over the tile's 128 keys. A is the dS^T tile (rows = keys,
+    // queries contiguous: MN-major for M = queries), B the item's K (rows = keys, head dim
+    // contiguous: MN-major for N = D); 16 keys (2 KB of rows) per instruction.
+    auto gemm_dq = [&](uint32_t d_tmem) {
+      const uint64_t a0 = make_sdesc_sw128(sbase + Plan::kDs, Plan::kChunkBytes, 1024);
+      const uint64_t b0 = make_sdesc_sw128(sX1, Plan::kChunkBytes, 1024);
+#pragma unroll
+      for (int kk = 0; kk < kBlockN / 16; ++kk) {
+        const uint32_t off = (uint32_t)(kk * 16 * 128) >> 4;
+        ptx::umma_ss_warp(d_tmem, a0 + off, b0 + off, idDq, kk > 0 ? 1u : 0u);
+      }
+    };
     const uint32_t tT1 = tmem + C::kT1, tT2 = tmem + C::kT2;
     const uint32_t tAcc1 = tmem + C::kAcc1, tAcc2 = tmem + C::kAcc2;
     Ring<NS> ring;
@@ -630,8 +750,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       bool valid;
       int st1, st2;
       bool first, last;  // first / last step of its item
+      int g;             // the step's index among this CTA's steps
     };
-    Pending pend{false, 0, 0, false, false};
+    Pending pend{false, 0, 0, false, false, 0};
     auto acquire = [&]() -> int {
       const int st = ring.stage;
       const uint32_t ph = ring.phase;
@@ -664,10 +785,29 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         }
         ptx::tc_commit_warp(bar(Plan::kT2Free + h));
       }
+      // The step's Q and dO tiles are not read after dK and dV.
       ptx::tc_commit_warp(bar(Plan::kRingEmpty + pd.st1));
       if (KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + pd.st2));
+      if constexpr (DQ) {
+        // Both halves of dS^T are in shared memory (the PdSFull waits above).
+        const int buf = pd.g % C::kDqBufs;
+        if (C::kDqInT2) {
+          // dQ overwrites T2: wait until the dV and dK GEMMs above have read P and dS there.
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            if (!W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u)) return false;
+            t2f_par ^= 1u << h;
+          }
+        } else if (pd.g >= C::kDqBufs) {  // the dQ warps read out this buffer's previous tile
+          if (!W.wait_warp(bar(Plan::kDqFree + buf), (uint32_t)(pd.g / C::kDqBufs - 1) & 1u)) return false;
+        }
+        ptx::tc_fence_after();
+        gemm_dq(tmem + (uint32_t)(C::kDq + buf * D));
+        ptx::tc_commit_warp(bar(Plan::kDqFull + buf));
+      }
       if (pd.last) {
         ptx::tc_commit_warp(bar(Plan::kAccFull));
+        if (DQ) ptx::tc_commit_warp(bar(Plan::kXEmpty));  // the dQ GEMM was the last reader of K
         ++items_accumulated;
       }
       return true;
@@ -679,8 +819,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       const BwdItem it = decode_bwd<KV, WIN, VAR>(t, p);
       if (it.nsteps == 0) continue;  // block past its sequence's end
       // Q pass: the elementwise warps copy the next item's X only after finishing this
-      // item's epilogue, which waits for the last A(); issue it before waiting for X.
-      if (!KV && pend.valid) {
+      // item's epilogue, which waits for the last A(); issue it before waiting for X. Fused
+      // form: the last dQ GEMM reads X (K), which is refilled only after it.
+      if ((!KV || DQ) && pend.valid) {
         if (!(ok = accumulate(pend))) break;
         pend.valid = false;
       }
@@ -711,8 +852,12 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
 #pragma unroll 1
           for (int h = 0; h < 2 && ok; ++h) {
             if (steps_issued > 0) {
-              if (!(ok = W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u))) break;
-              t2f_par ^= 1u << h;
+              if (C::kDqInT2) {  // the dQ warps read this half of dQ(s-1) out of T2
+                if (!(ok = W.wait_warp(bar(Plan::kDqFree + h), (uint32_t)(steps_issued - 1) & 1u))) break;
+              } else {
+                if (!(ok = W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u))) break;
+                t2f_par ^= 1u << h;
+              }
               ptx::tc_fence_after();
             }
             gemm_nt(tT2 + (uint32_t)(64 * h), sX2, tmem + C::kXdO,
@@ -724,8 +869,12 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           if (steps_issued > 0) {
 #pragma unroll 1
             for (int h = 0; h < 2 && ok; ++h) {
-              ok = W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u);
-              t2f_par ^= 1u << h;
+              if (C::kDqInT2) {
+                ok = W.wait_warp(bar(Plan::kDqFree + h), (uint32_t)(steps_issued - 1) & 1u);
+              } else {
+                ok = W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u);
+                t2f_par ^= 1u << h;
+              }
             }
             if (!ok) break;
             ptx::tc_fence_after();
@@ -735,14 +884,82 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           ptx::tc_commit_warp(bar(Plan::kT2Full + 1));
         }
         if (!KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + st2));  // V: only dP reads it
-        if (s == it.nsteps - 1) ptx::tc_commit_warp(bar(KV ? Plan::kXEmpty : Plan::kXTFree));  // last reads of X
-        pend = Pending{true, st1, st2, s == 0, s == it.nsteps - 1};
+        if (!DQ && s == it.nsteps - 1) ptx::tc_commit_warp(bar(KV ? Plan::kXEmpty : Plan::kXTFree));  // last reads of X
+        pend = Pending{true, st1, st2, s == 0, s == it.nsteps - 1, steps_issued};
         ++steps_issued;
       }
     }
     if (ok && pend.valid) ok = accumulate(pend);
     ptx::tc_commit_warp(bar(Plan::kDrain));
     if (lane == 0) drain_wait(bar(Plan::kDrain), 0, p.timeout_ns, p.status, p.host_flag);
+    __syncwarp();
+  } else if (DQ && warp >= C::kWarpDq) {
+    ptx::setmaxnreg_dec<C::kRegsDq>();
+    // ======================================================= dQ reduction ===
+    // Per step: the dQ tile of the step's query tile (TMEM, thread = query row) goes out in
+    // 32-column chunks through kDqStage shared-memory staging chunks (row r's 128 bytes with
+    // the 128-byte swizzle: 16-byte unit u at position u ^ (r & 7), the box layout of tmDq),
+    // and each chunk is added into the accumulator by one TMA reduce, issued by one thread.
+    // Rows past the map's row extent are dropped by the TMA unit; rows of a packed batch
+    // past the sequence's end add exact zeros (their P, hence dS, is 0). The TMEM columns
+    // are handed back (DqFree) as soon as they are in registers. Named barrier 1 (these
+    // 128 threads) orders the staging writes against the reduce that reads them.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const bool leader = warp == C::kWarpDq && lane == 0;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t stage0 = sbase + Plan::kStage + (uint32_t)r * 128;
+    int g = 0;       // steps of this CTA
+    int chunks = 0;  // staging chunks filled so far
+    bool ok = true;
+    ItemReader reader;
+    while (ok) {
+      int t;
+      if (!(ok = reader.next(W, bar(Plan::kItemFull), bar(Plan::kItemEmpty), items, true, t)) || t < 0) break;
+      const BwdItem it = decode_bwd<KV, WIN, VAR>(t, p);
+      if (it.nsteps == 0) continue;  // block past its sequence's end
+      const int nq = it.hi - it.lo;
+      for (int s = 0; s < it.nsteps && ok; ++s, ++g) {
+        const int ytile = it.lo + s % nq;
+        const int hy = it.hx * p.kv_group + s / nq;
+        const int buf = g % C::kDqBufs;
+        if (!(ok = W.wait_warp(bar(Plan::kDqFull + buf), (uint32_t)(g / C::kDqBufs) & 1u))) break;
+        ptx::tc_fence_after();
+        // Box coordinates in tmDq: (column, row, plane); plane = b * H + h, or h when packed.
+        const int y = (VAR ? it.s0 : 0) + ytile * kBlockM;
+        const int z = VAR ? hy : it.b * p.H + hy;
+        const uint32_t src = tmem + lane_off + (uint32_t)(C::kDq + buf * D);
+#pragma unroll 1
+        for (int ch = 0; ch < D / 32; ++ch, ++chunks) {
+          uint32_t v[32];
+          ptx::tmem_ld32(src + ch * 32, v);
+          ptx::tmem_wait_ld();
+          ptx::reg_fence32(v);
+          if (C::kDqInT2 ? (ch & 1) == 1 : ch == D / 32 - 1) {
+            ptx::tc_fence_before();  // d = 128: this 64-column half of T2; d = 64: the buffer
+            ptx::mbar_arrive(bar(Plan::kDqFree + (C::kDqInT2 ? ch >> 1 : buf)));
+          }
+          const int sb = chunks % C::kDqStage;
+          if (chunks >= C::kDqStage) {  // the reduce that last read chunk sb has read it
+            if (leader) ptx::bulk_wait_group_read1();
+            ptx::named_bar_sync(1, 128);
+          }
+          const uint32_t row_addr = stage0 + (uint32_t)sb * Plan::kChunkBytes;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            ptx::st_shared_v4(row_addr + (((uint32_t)u ^ (uint32_t)(r & 7)) << 4), v[4 * u], v[4 * u + 1],
+                              v[4 * u + 2], v[4 * u + 3]);
+          ptx::fence_proxy_async_smem();
+          ptx::named_bar_sync(1, 128);
+          if (leader) {
+            ptx::tma_reduce_add_3d(&tmDq, sbase + Plan::kStage + (uint32_t)sb * Plan::kChunkBytes, ch * 32, y, z);
+            ptx::bulk_commit_group();
+          }
+        }
+      }
+    }
+    // Every reduce must have read its staging chunk (and landed) before the CTA exits.
+    if (leader) ptx::bulk_wait_group0();
     __syncwarp();
   } else {
     ptx::setmaxnreg_dec<C::kRegsOther>();

@@ -85,7 +85,7 @@ struct DeviceState {
   int cc_major = 0, cc_minor = 0;
   unsigned attr_done = 0;  // bit per kernel instantiation
   unsigned attr_tile = 0;  // bit per tile-kernel instantiation
-  unsigned attr_bwd = 0;   // bit per backward kernel instantiation
+  unsigned long long attr_bwd = 0;  // bit per backward kernel instantiation
 };
 
 std::mutex g_mu;
@@ -253,6 +253,19 @@ int encode_map(CUtensorMap* m, const void* ptr, int dtype, int B, int H, int N, 
   CUresult r = g_encode(m, dtype == APEX_ATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                         4, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? APEX_ATTN_OK : APEX_ATTN_ERR_TENSOR_MAP;
+}
+
+// Fused backward: the fp32 dQ accumulator as `planes` planes of `rows` rows x D, for TMA
+// reduce-adds of 32-column x 128-row boxes (128 bytes per box row, 128-byte swizzle).
+int encode_acc_map(CUtensorMap* m, float* ptr, int D, long long rows, long long planes) {
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)planes};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 4, (cuuint64_t)rows * D * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)apex::kBlockM, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? APEX_ATTN_OK : APEX_ATTN_ERR_TENSOR_MAP;
 }
@@ -592,6 +605,21 @@ size_t bwd_workspace_bytes(int batch, int heads_q, int seqlen) {
   return (size_t)2 * (size_t)batch * (size_t)heads_q * (size_t)bwd_padded_rows(seqlen) * sizeof(float);
 }
 
+// Fused mode: the statistics, then (256-byte aligned) the fp32 dQ accumulator of
+// batch * heads_q * seqlen rows of head_dim (for a packed batch, seqlen = the longest
+// sequence, so the total token count fits).
+size_t bwd_dq_acc_offset(int batch, int heads_q, int seqlen) {
+  return (bwd_workspace_bytes(batch, heads_q, seqlen) + 255) / 256 * 256;
+}
+
+size_t bwd_workspace_bytes_mode(int batch, int heads_q, int seqlen, int head_dim, int mode) {
+  if (batch <= 0 || heads_q <= 0 || seqlen <= 0) return 0;
+  if (mode != APEX_ATTN_BWD_FUSED) return bwd_workspace_bytes(batch, heads_q, seqlen);
+  if (head_dim <= 0) return 0;
+  return bwd_dq_acc_offset(batch, heads_q, seqlen) +
+         (size_t)batch * (size_t)heads_q * (size_t)seqlen * (size_t)head_dim * sizeof(float);
+}
+
 // The backward's inputs in one shape for the batched and the packed entry points: strides
 // are (batch, head, row) element strides of q, k, v, o, dout, dq, dk, dv (batch stride 0
 // for a packed batch, whose rows are tokens).
@@ -604,15 +632,18 @@ struct BwdCall {
   long long st[24];
   const int* cu_seqlens;  // null: batched
   int total;
+  float* dq_acc;  // fused mode: the zeroed fp32 dQ accumulator; null: two passes
 };
 
-template <int D, typename T, bool KV, bool WIN, bool VAR>
+template <int D, typename T, bool KV, bool WIN, bool VAR, bool DQ>
 int launch_bwd_one(DeviceState& ds, const CUtensorMap& x1, const CUtensorMap& x2, const CUtensorMap& y1,
-                   const CUtensorMap& y2, const apex::BwdParams& p, int grid, cudaStream_t stream) {
-  auto kern = apex::attn_bwd_sm100_kernel<D, T, KV, WIN, VAR>;
-  constexpr int smem = apex::BwdSmem<D>::kDynamicBytes;
-  constexpr unsigned bit = 1u << ((VAR ? 16 : 0) + (D == 128 ? 8 : 0) + (std::is_same<T, __half>::value ? 4 : 0) +
-                                  (KV ? 2 : 0) + (WIN ? 1 : 0));
+                   const CUtensorMap& y2, const CUtensorMap& dqm, const apex::BwdParams& p, int grid,
+                   cudaStream_t stream) {
+  auto kern = apex::attn_bwd_sm100_kernel<D, T, KV, WIN, VAR, DQ>;
+  constexpr int smem = apex::BwdSmem<D, DQ>::kDynamicBytes;
+  // One bit per instantiation: VAR, d = 128, fp16 and DQ select a group of 4 (KV, WIN).
+  constexpr unsigned long long bit = 1ull << (((VAR ? 8 : 0) + (D == 128 ? 4 : 0) + (std::is_same<T, __half>::value ? 2 : 0) +
+                                   (DQ ? 1 : 0)) * 4 + (KV ? 2 : 0) + (WIN ? 1 : 0));
   if (!(ds.attr_bwd & bit)) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
@@ -621,18 +652,19 @@ int launch_bwd_one(DeviceState& ds, const CUtensorMap& x1, const CUtensorMap& x2
     }
     ds.attr_bwd |= bit;
   }
-  kern<<<grid, apex::BwdCfg<D>::kThreads, smem, stream>>>(x1, x2, y1, y2, p);
+  kern<<<grid, apex::BwdCfg<D, DQ>::kThreads, smem, stream>>>(x1, x2, y1, y2, dqm, p);
   if (cudaGetLastError() != cudaSuccess) return APEX_ATTN_ERR_LAUNCH;
   return APEX_ATTN_OK;
 }
 
-// Both passes of one direction (dK/dV or dQ), windowed or not.
-template <int D, typename T, bool KV, bool VAR>
+// One pass (dK/dV, fused dK/dV/dQ, or dQ), windowed or not. `dqm` is read by the fused
+// pass only (the others get any valid map).
+template <int D, typename T, bool KV, bool VAR, bool DQ = false>
 int launch_bwd_pass(DeviceState& ds, bool win, const CUtensorMap& x1, const CUtensorMap& x2,
-                    const CUtensorMap& y1, const CUtensorMap& y2, const apex::BwdParams& p, int grid,
-                    cudaStream_t s) {
-  return win ? launch_bwd_one<D, T, KV, true, VAR>(ds, x1, x2, y1, y2, p, grid, s)
-             : launch_bwd_one<D, T, KV, false, VAR>(ds, x1, x2, y1, y2, p, grid, s);
+                    const CUtensorMap& y1, const CUtensorMap& y2, const CUtensorMap& dqm,
+                    const apex::BwdParams& p, int grid, cudaStream_t s) {
+  return win ? launch_bwd_one<D, T, KV, true, VAR, DQ>(ds, x1, x2, y1, y2, dqm, p, grid, s)
+             : launch_bwd_one<D, T, KV, false, VAR, DQ>(ds, x1, x2, y1, y2, dqm, p, grid, s);
 }
 
 // Prep pass, then the dK/dV pass (K, V stationary) and the dQ pass (Q, dO stationary).
@@ -701,8 +733,34 @@ int launch_bwd(DeviceState& ds, const BwdCall& a, const CUtensorMap& mq, const C
     return APEX_ATTN_ERR_CUDA;
   }
   const int grid_kv = std::min(pk.num_items, ds.num_sms);
-  rc = var ? launch_bwd_pass<D, T, true, true>(ds, win, mk, mv, mq, mdo, pk, grid_kv, s)
-           : launch_bwd_pass<D, T, true, false>(ds, win, mk, mv, mq, mdo, pk, grid_kv, s);
+  if (a.dq_acc != nullptr) {
+    // Fused: one pass adds every step's dQ tile into the zeroed fp32 accumulator, then a
+    // cast writes dq = scale * acc.
+    const long long acc_rows = var ? (long long)a.heads_q * a.total : (long long)a.batch * a.heads_q * a.seqlen;
+    if (cudaMemsetAsync(a.dq_acc, 0, (size_t)acc_rows * D * sizeof(float), s) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return APEX_ATTN_ERR_CUDA;
+    }
+    pk.dq_acc = a.dq_acc;
+    CUtensorMap macc;
+    rc = var ? encode_acc_map(&macc, a.dq_acc, D, a.total, a.heads_q)
+             : encode_acc_map(&macc, a.dq_acc, D, a.seqlen, (long long)a.batch * a.heads_q);
+    if (rc != APEX_ATTN_OK) return rc;
+    rc = var ? launch_bwd_pass<D, T, true, true, true>(ds, win, mk, mv, mq, mdo, macc, pk, grid_kv, s)
+             : launch_bwd_pass<D, T, true, false, true>(ds, win, mk, mv, mq, mdo, macc, pk, grid_kv, s);
+    if (rc != APEX_ATTN_OK) return rc;
+    if (var)
+      apex::attn_bwd_dq_cast_kernel<T, D, true><<<blocks, 256, 0, s>>>(
+          a.dq_acc, static_cast<T*>(a.dq), 0, st[16], st[17], a.heads_q, a.seqlen, npad, rows, a.cu_seqlens,
+          a.total, a.sm_scale);
+    else
+      apex::attn_bwd_dq_cast_kernel<T, D, false><<<blocks, 256, 0, s>>>(
+          a.dq_acc, static_cast<T*>(a.dq), st[15], st[16], st[17], a.heads_q, a.seqlen, npad, rows, nullptr, 0,
+          a.sm_scale);
+    return cudaGetLastError() == cudaSuccess ? APEX_ATTN_OK : APEX_ATTN_ERR_LAUNCH;
+  }
+  rc = var ? launch_bwd_pass<D, T, true, true>(ds, win, mk, mv, mq, mdo, mk, pk, grid_kv, s)
+           : launch_bwd_pass<D, T, true, false>(ds, win, mk, mv, mq, mdo, mk, pk, grid_kv, s);
   if (rc != APEX_ATTN_OK) return rc;
   // dQ: items over (batch, query head, query block); K and V stream.
   apex::BwdParams pq = p;
@@ -715,17 +773,18 @@ int launch_bwd(DeviceState& ds, const BwdCall& a, const CUtensorMap& mq, const C
     return APEX_ATTN_ERR_CUDA;
   }
   const int grid_q = std::min(pq.num_items, ds.num_sms);
-  return var ? launch_bwd_pass<D, T, false, true>(ds, win, mq, mdo, mk, mv, pq, grid_q, s)
-             : launch_bwd_pass<D, T, false, false>(ds, win, mq, mdo, mk, mv, pq, grid_q, s);
+  return var ? launch_bwd_pass<D, T, false, true>(ds, win, mq, mdo, mk, mv, mq, pq, grid_q, s)
+             : launch_bwd_pass<D, T, false, false>(ds, win, mq, mdo, mk, mv, mq, pq, grid_q, s);
 }
 
 int dispatch_bwd(DeviceState& ds, const BwdCall& call, int head_dim, int dtype, const CUtensorMap& mq,
                  const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo, void* workspace,
                  long long npad, void* stream);
 
-int backward(const apex_attn_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+int backward(const apex_attn_bwd_args* a, int mode, void* workspace, size_t workspace_bytes, void* stream) {
   // ---- argument validation (no CUDA calls) ----
   if (!a) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (mode != APEX_ATTN_BWD_DETERMINISTIC && mode != APEX_ATTN_BWD_FUSED) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv || !workspace)
     return APEX_ATTN_ERR_INVALID_ARGUMENT;
   if (a->batch <= 0 || a->heads_q <= 0 || a->seqlen <= 0) return APEX_ATTN_ERR_INVALID_ARGUMENT;
@@ -746,7 +805,8 @@ int backward(const apex_attn_bwd_args* a, void* workspace, size_t workspace_byte
   for (const void* ptr : ptrs)
     if (!aligned16(ptr)) return APEX_ATTN_ERR_BAD_LAYOUT;
   if ((reinterpret_cast<uintptr_t>(a->lse) & 3u) || !aligned16(workspace)) return APEX_ATTN_ERR_BAD_LAYOUT;
-  if (workspace_bytes < bwd_workspace_bytes(a->batch, a->heads_q, a->seqlen)) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < bwd_workspace_bytes_mode(a->batch, a->heads_q, a->seqlen, a->head_dim, mode))
+    return APEX_ATTN_ERR_INVALID_ARGUMENT;
 
   // ---- device ----
   const int dev = device_of(a->q);
@@ -768,8 +828,10 @@ int backward(const apex_attn_bwd_args* a, void* workspace, size_t workspace_byte
       (rc = encode_map(&mdo, a->dout, a->dtype, B, H, N, D, st[12], st[13], st[14])))
     return rc;
   BwdCall call{a->o, a->dout, a->lse, a->dq, a->dk, a->dv, B, H, HKV, N, a->causal, a->window_left,
-               a->sm_scale, {}, nullptr, 0};
+               a->sm_scale, {}, nullptr, 0, nullptr};
   for (int i = 0; i < 24; ++i) call.st[i] = st[i];
+  if (mode == APEX_ATTN_BWD_FUSED)
+    call.dq_acc = reinterpret_cast<float*>(static_cast<char*>(workspace) + bwd_dq_acc_offset(B, H, N));
   return dispatch_bwd(*ds, call, a->head_dim, a->dtype, mq, mk, mv, mdo, workspace, npad, stream);
 }
 
@@ -788,9 +850,11 @@ int dispatch_bwd(DeviceState& ds, const BwdCall& call, int head_dim, int dtype, 
 }
 
 // Packed variable-length backward (apex_attn_bwd_varlen).
-int backward_varlen(const apex_attn_bwd_varlen_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+int backward_varlen(const apex_attn_bwd_varlen_args* a, int mode, void* workspace, size_t workspace_bytes,
+                    void* stream) {
   // ---- argument validation (no CUDA calls) ----
   if (!a) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (mode != APEX_ATTN_BWD_DETERMINISTIC && mode != APEX_ATTN_BWD_FUSED) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv ||
       !a->cu_seqlens || !workspace)
     return APEX_ATTN_ERR_INVALID_ARGUMENT;
@@ -814,7 +878,12 @@ int backward_varlen(const apex_attn_bwd_varlen_args* a, void* workspace, size_t 
   if ((reinterpret_cast<uintptr_t>(a->lse) & 3u) || (reinterpret_cast<uintptr_t>(a->cu_seqlens) & 3u) ||
       !aligned16(workspace))
     return APEX_ATTN_ERR_BAD_LAYOUT;
-  if (workspace_bytes < bwd_workspace_bytes(a->batch, a->heads_q, a->max_seqlen)) return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  // The fused mode's accumulator holds heads_q x total rows; total <= batch x max_seqlen
+  // for valid offsets, and the size asked for covers batch x max_seqlen.
+  if (mode == APEX_ATTN_BWD_FUSED && (long long)a->total > (long long)a->batch * a->max_seqlen)
+    return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < bwd_workspace_bytes_mode(a->batch, a->heads_q, a->max_seqlen, a->head_dim, mode))
+    return APEX_ATTN_ERR_INVALID_ARGUMENT;
 
   // ---- device ----
   const int dev = device_of(a->q);
@@ -838,7 +907,10 @@ int backward_varlen(const apex_attn_bwd_varlen_args* a, void* workspace, size_t 
       (rc = encode_map(&mdo, a->dout, a->dtype, 1, a->heads_q, T, D, 0, st[9], st[8])))
     return rc;
   BwdCall call{a->o, a->dout, a->lse, a->dq, a->dk, a->dv, a->batch, a->heads_q, a->heads_kv,
-               a->max_seqlen, a->causal, a->window_left, a->sm_scale, {}, a->cu_seqlens, a->total};
+               a->max_seqlen, a->causal, a->window_left, a->sm_scale, {}, a->cu_seqlens, a->total, nullptr};
+  if (mode == APEX_ATTN_BWD_FUSED)
+    call.dq_acc = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                           bwd_dq_acc_offset(a->batch, a->heads_q, a->max_seqlen));
   for (int t = 0; t < 8; ++t) {  // (batch, head, row) per tensor; no batch stride when packed
     call.st[3 * t] = 0;
     call.st[3 * t + 1] = st[2 * t + 1];
@@ -855,13 +927,27 @@ size_t apex_attn_bwd_workspace_bytes(int batch, int heads_q, int seqlen) {
   return bwd_workspace_bytes(batch, heads_q, seqlen);
 }
 
+size_t apex_attn_bwd_workspace_bytes_mode(int batch, int heads_q, int seqlen, int head_dim, int mode) {
+  return bwd_workspace_bytes_mode(batch, heads_q, seqlen, head_dim, mode);
+}
+
 int apex_attn_bwd(const apex_attn_bwd_args* args, void* workspace, size_t workspace_bytes, void* stream) {
-  return backward(args, workspace, workspace_bytes, stream);
+  return backward(args, APEX_ATTN_BWD_DETERMINISTIC, workspace, workspace_bytes, stream);
+}
+
+int apex_attn_bwd_mode(const apex_attn_bwd_args* args, int mode, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  return backward(args, mode, workspace, workspace_bytes, stream);
 }
 
 int apex_attn_bwd_varlen(const apex_attn_bwd_varlen_args* args, void* workspace, size_t workspace_bytes,
                          void* stream) {
-  return backward_varlen(args, workspace, workspace_bytes, stream);
+  return backward_varlen(args, APEX_ATTN_BWD_DETERMINISTIC, workspace, workspace_bytes, stream);
+}
+
+int apex_attn_bwd_varlen_mode(const apex_attn_bwd_varlen_args* args, int mode, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  return backward_varlen(args, mode, workspace, workspace_bytes, stream);
 }
 
 int apex_attn_version(void) { return kVersion; }

@@ -148,10 +148,11 @@ struct DType<__half> {
 
 // UMMA instruction descriptor, kind::f16, fp32 accumulate, dense.
 template <typename T>
-__host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool b_mn_major) {
+__host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool b_mn_major, bool a_mn_major = false) {
   return (1u << 4)                               // D format: F32
          | (DType<T>::kUmmaFormat << 7)          // A format
          | (DType<T>::kUmmaFormat << 10)         // B format
+         | ((a_mn_major ? 1u : 0u) << 15)        // A major-ness (shared-memory A only)
          | ((b_mn_major ? 1u : 0u) << 16)        // B major-ness
          | ((uint32_t)(N >> 3) << 17)            // N / 8
          | ((uint32_t)(M >> 4) << 24);           // M / 16

@@ -100,8 +100,28 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// Waits until the shared-memory sources of all but the newest committed bulk group were read.
+__device__ __forceinline__ void bulk_wait_group_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
 // Waits until every committed bulk group completed (global writes done).
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Element-wise add of a shared-memory box into global memory at box coordinates (x, y, z)
+// of a 3-D tensor map (the add happens at the L2; the element type is the map's).
+__device__ __forceinline__ void tma_reduce_add_3d(const void* tmap, uint32_t src, int x, int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(src), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Named barrier `id` (1-15; 0 is __syncthreads) over `count` threads, a multiple of 32.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -339,6 +359,14 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 // (tensor-core operand reads) ordered after a subsequent barrier arrive.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------------------------------------ global memory --
+// Adds four consecutive floats into global memory at the L2 (16-byte aligned address; no
+// value returned, relaxed ordering).
+__device__ __forceinline__ void red_add_v4_f32(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
 }
 
 // ------------------------------------------------------------ misc math -----

@@ -300,7 +300,11 @@ def bench_backward(name, c, steps, warmup, device):
     o, lse = custom_attention_forward(q, k, v, causal=True, return_lse=True)
     ms, _ = time_device(lambda: custom_attention_backward(q, k, v, o, lse, do, causal=True),
                         steps, warmup, stream)
-    dq, dk, dv = custom_attention_backward(q, k, v, o, lse, do, causal=True)
+    ms_fused, _ = time_device(lambda: custom_attention_backward(q, k, v, o, lse, do, causal=True,
+                                                                deterministic=False),
+                              steps, warmup, stream)
+    grads = custom_attention_backward(q, k, v, o, lse, do, causal=True)
+    grads_fused = custom_attention_backward(q, k, v, o, lse, do, causal=True, deterministic=False)
     # parity on one head
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -310,11 +314,15 @@ def bench_backward(name, c, steps, warmup, device):
         torch.ones(n, n, dtype=torch.bool, device=device).triu(1), float("-inf"))
     (torch.softmax(s, dim=-1) @ vh).backward(do[0, 0].float())
     torch.backends.cuda.matmul.allow_tf32 = prev
-    ratio = 0.0
-    for got, ref in ((dq, qh.grad), (dk, kh.grad), (dv, vh.grad)):
-        bound = 2.5e-2 + 2.0 ** -7 * ref.abs()
-        ratio = max(ratio, ((got[0, 0].float() - ref).abs() / bound).max().item())
-    del s, qh, kh, vh
+
+    def worst(gs):
+        r = 0.0
+        for got, ref in zip(gs, (qh.grad, kh.grad, vh.grad)):
+            bound = 2.5e-2 + 2.0 ** -7 * ref.abs()
+            r = max(r, ((got[0, 0].float() - ref).abs() / bound).max().item())
+        return r
+    ratio, ratio_fused = worst(grads), worst(grads_fused)
+    del s, qh, kh, vh, grads, grads_fused
     # torch SDPA backward on the same inputs
     qs, ks, vs = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
     os_ = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True)
@@ -323,13 +331,21 @@ def bench_backward(name, c, steps, warmup, device):
     f = 2.5 * flops(c)
     peaks, _ = load_peaks()
     t = f * steps / (ms * 1e-3) / 1e12
+    tf = f * steps / (ms_fused * 1e-3) / 1e12
     ts = f * steps / (sdpa_ms * 1e-3) / 1e12
     return {"config": c, "tflops": round(t, 1), "ms_per_step": round(ms / steps, 4),
             "frac_of_peak": round(t / peaks["bf16_tflops"], 4),
             "sdpa_tflops_same_gpu": round(ts, 1), "speedup_vs_sdpa": round(t / ts, 3),
             "flop_per_step": f, "flop_convention": "2.5 x forward (5 GEMMs of 2 N^2 d / 2, causal)",
             "parity_worst_err_over_bound": round(ratio, 3),
-            "launches_per_step": "prep + dK/dV pass + dQ pass (+ 2 counter memsets)"}
+            "launches_per_step": "prep + dK/dV pass + dQ pass (+ 2 counter memsets)",
+            "fused": {"tflops": round(tf, 1), "ms_per_step": round(ms_fused / steps, 4),
+                      "frac_of_peak": round(tf / peaks["bf16_tflops"], 4),
+                      "speedup_vs_sdpa": round(tf / ts, 3),
+                      "parity_worst_err_over_bound": round(ratio_fused, 3),
+                      "launches_per_step": "prep + fused dK/dV/dQ pass + dq cast (+ counter and "
+                                           "accumulator memsets)",
+                      "deterministic": False}}
 
 
 def pipelined_e2e(host_in, op, steps, warmup, device):
@@ -591,6 +607,8 @@ def main():
                     help="run only the device-resident kernel leg of one config (profiling)")
     ap.add_argument("--only-bwd", choices=sorted(BWD_PROFILE_CONFIGS), default=None,
                     help="run only the backward of one config, device-resident (profiling)")
+    ap.add_argument("--bwd-fused", action="store_true",
+                    help="with --only-bwd: time the fused one-pass backward instead of the default")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -644,11 +662,13 @@ def main():
         q, k, v = make_device_inputs(c, 7, device)
         do = torch.randn(q.shape, device=device, dtype=torch.float32).to(torch.bfloat16)
         o, lse = custom_attention_forward(q, k, v, causal=True, return_lse=True)
-        ms, _ = time_device(lambda: custom_attention_backward(q, k, v, o, lse, do, causal=True),
+        det = not args.bwd_fused
+        ms, _ = time_device(lambda: custom_attention_backward(q, k, v, o, lse, do, causal=True,
+                                                              deterministic=det),
                             args.steps, args.warmup, torch.cuda.current_stream(device))
         t = 2.5 * flops(c) * args.steps / (ms * 1e-3) / 1e12
-        print(json.dumps({"backward": args.only_bwd, **c, "tflops": t, "ms_per_step": ms / args.steps,
-                          "device_status": apex_attn.device_status()}))
+        print(json.dumps({"backward": args.only_bwd, **c, "fused": not det, "tflops": t,
+                          "ms_per_step": ms / args.steps, "device_status": apex_attn.device_status()}))
         return
     if args.only:
         c = CONFIGS[args.only]

@@ -227,7 +227,8 @@ int apex_attn_noalloc_status(int device, int* flags);
  * workspace: device memory of at least apex_attn_bwd_workspace_bytes(batch, heads_q,
  * seqlen) bytes, 16-byte aligned, on the same device; used only during the call (it holds
  * two fp32 values per query row). Smaller: APEX_ATTN_ERR_INVALID_ARGUMENT.
- * Asynchronous on `stream`; results are deterministic (no atomics).
+ * Asynchronous on `stream`; results are deterministic (no atomics). apex_attn_bwd_mode
+ * selects the faster fused algorithm instead.
  *
  * Replaces: _flash_attn_bwd(q, k, v, out, grad_output, lse, causal=True,
  * window_size_left=w), the backward that nanochat's attention custom op calls
@@ -260,6 +261,31 @@ size_t apex_attn_bwd_workspace_bytes(int batch, int heads_q, int seqlen);
 
 int apex_attn_bwd(const apex_attn_bwd_args* args, void* workspace, size_t workspace_bytes,
                   void* stream);
+
+/*
+ * Backward algorithms (the `mode` of apex_attn_bwd_mode / apex_attn_bwd_varlen_mode):
+ *   APEX_ATTN_BWD_DETERMINISTIC  what apex_attn_bwd runs: a dK/dV pass and a dQ pass that
+ *                                recomputes the scores; bitwise reproducible.
+ *   APEX_ATTN_BWD_FUSED          one pass: each (key block, query tile) step also computes
+ *                                its dQ tile and adds it into an fp32 accumulator in the
+ *                                workspace with global reductions, then a cast writes dq.
+ *                                Five GEMMs per step instead of seven; dk and dv are
+ *                                bitwise the same as in the deterministic mode, dq is not
+ *                                reproducible bit for bit (the reductions' order varies).
+ * Any other mode: APEX_ATTN_ERR_INVALID_ARGUMENT.
+ */
+#define APEX_ATTN_BWD_DETERMINISTIC 0
+#define APEX_ATTN_BWD_FUSED 1
+
+/* Workspace bytes for `mode` (0 for non-positive sizes). The fused mode adds an fp32
+ * accumulator of batch * heads_q * seqlen * head_dim values; for a packed batch pass
+ * max_seqlen as seqlen. */
+size_t apex_attn_bwd_workspace_bytes_mode(int batch, int heads_q, int seqlen, int head_dim, int mode);
+
+/* apex_attn_bwd with the algorithm chosen by `mode`; workspace as
+ * apex_attn_bwd_workspace_bytes_mode(batch, heads_q, seqlen, head_dim, mode). */
+int apex_attn_bwd_mode(const apex_attn_bwd_args* args, int mode, void* workspace,
+                       size_t workspace_bytes, void* stream);
 
 /*
  * Backward of apex_attn_fwd_varlen: dq, dk, dv of a packed variable-length batch.
@@ -297,6 +323,13 @@ typedef struct apex_attn_bwd_varlen_args {
 
 int apex_attn_bwd_varlen(const apex_attn_bwd_varlen_args* args, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/* apex_attn_bwd_varlen with the algorithm chosen by `mode` (see apex_attn_bwd_mode);
+ * workspace as apex_attn_bwd_workspace_bytes_mode(batch, heads_q, max_seqlen, head_dim,
+ * mode). The fused mode needs total <= batch * max_seqlen (true of any valid cu_seqlens),
+ * else APEX_ATTN_ERR_INVALID_ARGUMENT. */
+int apex_attn_bwd_varlen_mode(const apex_attn_bwd_varlen_args* args, int mode, void* workspace,
+                              size_t workspace_bytes, void* stream);
 
 /* Number of SMs of `device` (the persistent kernels' grid is min(work items, this)), or a
  * negative status: APEX_ATTN_ERR_NO_DEVICE for a bad ordinal or no device,

@@ -277,6 +277,39 @@ def test_bwd_varlen_workspace_checks(lib):
     assert lib.apex_attn_bwd_varlen(None, FAKE, need, None) == _lib.ERR_INVALID_ARGUMENT
 
 
+# ----------------------------------------------------- backward modes --------
+def test_bwd_workspace_bytes_by_mode(lib):
+    """Mode 0 (deterministic) needs what apex_attn_bwd needs; mode 1 (fused) adds a
+    256-byte-aligned fp32 dQ accumulator of batch * heads * seqlen * head_dim values."""
+    for b, h, n, d in ((2, 3, 130, 64), (1, 1, 128, 128), (4, 32, 8192, 128)):
+        base = lib.apex_attn_bwd_workspace_bytes(b, h, n)
+        assert lib.apex_attn_bwd_workspace_bytes_mode(b, h, n, d, 0) == base
+        assert lib.apex_attn_bwd_workspace_bytes_mode(b, h, n, d, 1) == (base + 255) // 256 * 256 + b * h * n * d * 4
+    assert lib.apex_attn_bwd_workspace_bytes_mode(0, 3, 130, 64, 1) == 0
+    assert lib.apex_attn_bwd_workspace_bytes_mode(1, 1, 128, 0, 1) == 0
+
+
+def test_bwd_mode_validation(lib):
+    a = _bwd_args()
+    det = lib.apex_attn_bwd_workspace_bytes_mode(1, 4, 256, 64, 0)
+    fused = lib.apex_attn_bwd_workspace_bytes_mode(1, 4, 256, 64, 1)
+    for bad in (-1, 2, 7):
+        assert lib.apex_attn_bwd_mode(ctypes.byref(a), bad, FAKE, fused, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.apex_attn_bwd_mode(ctypes.byref(a), 1, FAKE, det, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.apex_attn_bwd_mode(ctypes.byref(a), 1, FAKE, fused - 4, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.apex_attn_bwd_mode(None, 1, FAKE, fused, None) == _lib.ERR_INVALID_ARGUMENT
+    # valid arguments reach the device lookup, which fails on host (fake) pointers
+    assert lib.apex_attn_bwd_mode(ctypes.byref(a), 1, FAKE, fused, None) == _lib.ERR_NO_DEVICE
+    v = _bwd_varlen_args()
+    vf = lib.apex_attn_bwd_workspace_bytes_mode(3, 4, 500, 128, 1)
+    assert lib.apex_attn_bwd_varlen_mode(ctypes.byref(v), 3, FAKE, vf, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.apex_attn_bwd_varlen_mode(ctypes.byref(v), 1, FAKE, vf - 16, None) == _lib.ERR_INVALID_ARGUMENT
+    # the accumulator holds heads x total rows, which batch x max_seqlen must cover
+    big = _bwd_varlen_args(total=1501)
+    assert lib.apex_attn_bwd_varlen_mode(ctypes.byref(big), 1, FAKE, 1 << 30, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.apex_attn_bwd_varlen_mode(ctypes.byref(v), 1, FAKE, vf, None) == _lib.ERR_NO_DEVICE
+
+
 def test_num_sms_hint_without_device(lib):
     import torch
     if torch.cuda.is_available():
