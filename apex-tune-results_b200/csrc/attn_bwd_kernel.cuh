@@ -190,7 +190,8 @@ struct BwdSmem {
   static constexpr int kDqFull = kDrain + 1;    // [2] fused form: dQ tile in TMEM buffer b
   // [2] fused form: dQ buffer b read out (d = 128: 64-column half b of the one buffer)
   static constexpr int kDqFree = kDqFull + 2;
-  static constexpr int kItemFull = kDqFree + 2;
+  static constexpr int kDsFree = kDqFree + 2;   // fused form, d = 64: the dQ GEMM read the dS tile
+  static constexpr int kItemFull = kDsFree + 1;
   static constexpr int kItemEmpty = kItemFull + kItemRing;
   static constexpr int kNumBars = kItemEmpty + kItemRing;
   static constexpr int kItems = kBars + kNumBars * 8;
@@ -423,6 +424,7 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
       ptx::mbar_init(bar(Plan::kDqFull + b), 1);
       ptx::mbar_init(bar(Plan::kDqFree + b), 128);
     }
+    ptx::mbar_init(bar(Plan::kDsFree), 1);
     // Item-ring readers: the 8 elementwise warps, the MMA warp (and the 4 dQ warps).
     for (int k = 0; k < kItemRing; ++k) {
       ptx::mbar_init(bar(Plan::kItemFull + k), 1);
@@ -627,6 +629,10 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
             }
             ptx::tmem_st32(tT2 + 32, pk_s);  // dS_h after P_h
             if (DQ) {
+              // At d = 64 the previous step's dQ GEMM may still be reading the dS tile (it is
+              // issued after this step's dP GEMM); at d = 128 it completed before dP (T2).
+              if (!C::kDqInT2 && gstep > 0 && !(ok = W.wait_warp(bar(Plan::kDsFree), (uint32_t)(gstep - 1) & 1u)))
+                break;
               // The same dS^T row into the shared-memory tile of the dQ GEMM: chunk `half`
               // (queries 64 half ..), row r, 16-byte unit u at position u ^ (r & 7).
               const uint32_t drow = sbase + Plan::kDs + half * Plan::kChunkBytes + r * 128;
@@ -762,6 +768,25 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
       return st;
     };
     // A(step): accumulating GEMMs of a step whose G1, G2 were issued earlier.
+    // Fused form: dQ(step) = dS K into the step's dQ buffer. Both halves of dS^T are in
+    // shared memory (accumulate() waited for them). At d = 128 accumulate() issues it
+    // right after dV and dK (it reuses T2); at d = 64 the main loop issues it after the
+    // next step's dP GEMM, which the elementwise warps wait for, and the elementwise warps
+    // wait for kDsFree before they overwrite the dS tile.
+    auto issue_dq = [&](const Pending& pd) -> bool {
+      if constexpr (DQ) {
+        const int buf = pd.g % C::kDqBufs;
+        if (!C::kDqInT2 && pd.g >= C::kDqBufs) {  // the dQ warps read out this buffer's previous tile
+          if (!W.wait_warp(bar(Plan::kDqFree + buf), (uint32_t)(pd.g / C::kDqBufs - 1) & 1u)) return false;
+          ptx::tc_fence_after();
+        }
+        gemm_dq(tmem + (uint32_t)(C::kDq + buf * D));
+        ptx::tc_commit_warp(bar(Plan::kDqFull + buf));
+        if (!C::kDqInT2) ptx::tc_commit_warp(bar(Plan::kDsFree));
+        if (pd.last) ptx::tc_commit_warp(bar(Plan::kXEmpty));  // the dQ GEMM was the last reader of K
+      }
+      return true;
+    };
     auto accumulate = [&](const Pending& pd) -> bool {
       if (pd.first && items_accumulated > 0) {  // the epilogue must have drained the accumulators
         if (!W.wait_warp(bar(Plan::kAccEmpty), ae_par)) return false;
@@ -788,27 +813,19 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
       // The step's Q and dO tiles are not read after dK and dV.
       ptx::tc_commit_warp(bar(Plan::kRingEmpty + pd.st1));
       if (KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + pd.st2));
-      if constexpr (DQ) {
-        // Both halves of dS^T are in shared memory (the PdSFull waits above).
-        const int buf = pd.g % C::kDqBufs;
-        if (C::kDqInT2) {
-          // dQ overwrites T2: wait until the dV and dK GEMMs above have read P and dS there.
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            if (!W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u)) return false;
-            t2f_par ^= 1u << h;
-          }
-        } else if (pd.g >= C::kDqBufs) {  // the dQ warps read out this buffer's previous tile
-          if (!W.wait_warp(bar(Plan::kDqFree + buf), (uint32_t)(pd.g / C::kDqBufs - 1) & 1u)) return false;
-        }
-        ptx::tc_fence_after();
-        gemm_dq(tmem + (uint32_t)(C::kDq + buf * D));
-        ptx::tc_commit_warp(bar(Plan::kDqFull + buf));
-      }
       if (pd.last) {
         ptx::tc_commit_warp(bar(Plan::kAccFull));
-        if (DQ) ptx::tc_commit_warp(bar(Plan::kXEmpty));  // the dQ GEMM was the last reader of K
         ++items_accumulated;
+      }
+      if constexpr (C::kDqInT2) {
+        // dQ overwrites T2: wait until the dV and dK GEMMs above have read P and dS there.
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          if (!W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u)) return false;
+          t2f_par ^= 1u << h;
+        }
+        ptx::tc_fence_after();
+        return issue_dq(pd);
       }
       return true;
     };
@@ -823,6 +840,7 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
       // form: the last dQ GEMM reads X (K), which is refilled only after it.
       if ((!KV || DQ) && pend.valid) {
         if (!(ok = accumulate(pend))) break;
+        if (DQ && !C::kDqInT2 && !(ok = issue_dq(pend))) break;
         pend.valid = false;
       }
       if (!(ok = W.wait_warp(bar(KV ? Plan::kXFull : Plan::kXTFull), x_par))) break;
@@ -839,8 +857,10 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         }
         gemm_nt(tT1, sX1, tmem + C::kXQ, sRing + st1 * Plan::kTileBytes, idNT);
         ptx::tc_commit_warp(bar(Plan::kT1Full));
+        Pending dq_next{false, 0, 0, false, false, 0};  // d = 64: dQ issued after this dP
         if (pend.valid) {
           if (!(ok = accumulate(pend))) break;
+          if (DQ && !C::kDqInT2) dq_next = pend;
           pend.valid = false;
         }
         const int st2 = acquire();
@@ -883,13 +903,17 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
           ptx::tc_commit_warp(bar(Plan::kT2Full));
           ptx::tc_commit_warp(bar(Plan::kT2Full + 1));
         }
+        if (dq_next.valid && !(ok = issue_dq(dq_next))) break;
         if (!KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + st2));  // V: only dP reads it
         if (!DQ && s == it.nsteps - 1) ptx::tc_commit_warp(bar(KV ? Plan::kXEmpty : Plan::kXTFree));  // last reads of X
         pend = Pending{true, st1, st2, s == 0, s == it.nsteps - 1, steps_issued};
         ++steps_issued;
       }
     }
-    if (ok && pend.valid) ok = accumulate(pend);
+    if (ok && pend.valid) {
+      ok = accumulate(pend);
+      if (ok && DQ && !C::kDqInT2) ok = issue_dq(pend);
+    }
     ptx::tc_commit_warp(bar(Plan::kDrain));
     if (lane == 0) drain_wait(bar(Plan::kDrain), 0, p.timeout_ns, p.status, p.host_flag);
     __syncwarp();
