@@ -88,6 +88,15 @@ struct AttnParams {
 #define APEX_FWD_ROWSPLIT128 0
 #endif
 
+// d = 128: P written into TMEM over the first 64 columns of its own S (instead of a shared-
+// memory P buffer). Each sub-tile's next S then waits for its P V, and the freed 64 KB of
+// shared memory take the K/V ring from 3 to 5 stages. Off: correct, but measured 18-25 %
+// slower (C3 969-985 vs 1179-1215 TFLOP/s): with one MMA warp per sub-tile the two
+// sub-tiles fall into step, each softmax idling while its P V and next S run.
+#ifndef APEX_FWD_PALIAS128
+#define APEX_FWD_PALIAS128 0
+#endif
+
 // WIN: the configuration of windowed launches (see kCS).
 template <int D, bool WIN = false>
 struct Cfg {
@@ -103,15 +112,18 @@ struct Cfg {
   static constexpr int kCS = D == 64 ? APEX_FWD_CS64 : ((D == 128 && !WIN && APEX_FWD_ROWSPLIT128) ? 2 : 1);
   static constexpr bool kRowSplit = kCS == 2 && !WIN;
   static constexpr int kLSlots = kCS == 2 && !kRowSplit ? 2 : 1;  // row-sum slots per sub-tile
-  static constexpr bool kPInTmem = D != 128;             // else P lives in shared memory
+  static constexpr bool kPAlias = D == 128 && APEX_FWD_PALIAS128;  // P over S (see above)
+  static constexpr bool kPInTmem = D != 128 || kPAlias;  // else P lives in shared memory
   static constexpr int kParts = D == 256 ? 2 : 1;        // ring stages per K or V tile
   static constexpr int kStageCols = D / kParts;          // head-dim columns per stage
-  static constexpr int kNS = D == 64 ? 8 : (D == 128 ? 3 : 5);  // ring stages
+  static constexpr int kNS = D == 64 ? 8 : (D == 128 ? (kPAlias ? 5 : 3) : 5);  // ring stages
   static constexpr int kThreads = 128 * (kSub * kCS + 2);
   static constexpr int kItemRows = kSub * kBlockM;
-  // TMEM columns: S_i at i*128; O_i at kTmemO + i*D; P_i at kTmemP + i*64 (TMEM variants).
+  // TMEM columns: S_i at i*128; O_i at kTmemO + i*D; P_i at kTmemP + i*kPStride (TMEM
+  // variants; with kPAlias, P_i is S_i's first 64 columns).
   static constexpr int kTmemO = 256;
-  static constexpr int kTmemP = D == 64 ? 384 : 128;
+  static constexpr int kTmemP = D == 64 ? 384 : (kPAlias ? 0 : 128);
+  static constexpr int kPStride = kPAlias ? 128 : 64;
   // setmaxnreg budgets (multiples of 8): softmax, epilogue, the remaining warpgroup. Their
   // sum x 128 must not exceed the launch allocation (kThreads x (65536 / kThreads)), or
   // setmaxnreg.inc would wait forever; checked below.
@@ -123,7 +135,7 @@ struct Cfg {
                 "setmaxnreg split exceeds the launch register allocation");
   static_assert(kCS == 1 || kPInTmem || kRowSplit, "split softmax columns need P in TMEM");
   static_assert(kTmemO + kSub * D <= 512, "TMEM plan overflows 512 columns");
-  static_assert(!kPInTmem || kTmemP + kSub * 64 <= kTmemO || kTmemP >= kTmemO + kSub * D,
+  static_assert(!kPInTmem || kTmemP + kSub * kPStride <= kTmemO || kTmemP >= kTmemO + kSub * D,
                 "P columns overlap O");
 };
 
@@ -378,7 +390,8 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, unsign
 // Position in the K/V ring, as every consumer and the producer walk it. Per item the
 // fills are K(0); then for j = 0 .. nbmax-1: K(j+1) (if j+1 < nbmax), V(j); each K or V
 // tile takes kParts consecutive stages. K runs one tile ahead of V because S(j+1) is
-// issued at the start of softmax(j) while P(j) V(j) waits for its end.
+// issued at the start of softmax(j) while P(j) V(j) waits for its end. With kPAlias the
+// order is V(j), then K(j+1): S(j+1) overwrites P(j), so it follows P(j) V(j).
 template <int NS>
 struct Ring {
   int stage = 0;
@@ -518,7 +531,7 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
       const uint32_t lane_off = (uint32_t)lb << 16;
       const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128);
       const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
-      const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64);
+      const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * C::kPStride);
       // P in shared memory (d = 128): the SW128 K-major tile of the sub-tile, keys 0-63 and
       // 64-127 in two 16 KB chunks; 16-byte unit u of row R sits at unit position
       // u ^ (R & 7). This thread writes the 4-byte word (lane % 4) of its units.
@@ -691,7 +704,7 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
       const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
       const uint32_t tS = tmem + lane_off + (uint32_t)(i * 128 + cs * kCols);
       const uint32_t tO = tmem + lane_off + (uint32_t)(C::kTmemO + i * D);
-      const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * 64 + cs * (kCols / 2));
+      const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * C::kPStride + cs * (kCols / 2));
       float* xch = reinterpret_cast<float*>(smem + Plan::kXch);  // [SUB][CS][2][128]
       int tcount = 0;  // tiles this warpgroup processed (row-max exchange slot and parity)
       // Row r of P in shared memory: two 16 KB chunks (keys 0-63, 64-127) of the SW128
@@ -924,7 +937,7 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
       const uint32_t sPi = sbase + Plan::kP + i * Plan::kPTileBytes;
       const uint32_t tSi = tmem + (uint32_t)(i * 128);
       const uint32_t tOi = tmem + (uint32_t)(C::kTmemO + i * D);
-      const uint32_t tPi = tmem + (uint32_t)(C::kTmemP + i * 64);
+      const uint32_t tPi = tmem + (uint32_t)(C::kTmemP + i * C::kPStride);
       Ring<NS> ring;
       uint32_t q_par = 0, sf_par = 0, pf_par = 0, oe_par = 0;  // O-empty is first waited on for item 2
       int s_issued = 0;    // S tiles issued (the S buffer is reused every tile)
@@ -943,10 +956,18 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
         __syncwarp();
       };
       // S_i(j): kParts stages of K, each contributing its head-dim slice.
+      bool pv_pending = false;  // kPAlias: a P V of this sub-tile may still be reading P (= S)
+      uint32_t pvf_par = 0;
       auto do_S = [&](bool needed) -> bool {
         if (needed && s_issued > 0) {
           if (!W.wait_warp(bar(Plan::kSFree + i), sf_par)) return false;
           sf_par ^= 1;
+        }
+        if (C::kPAlias && needed && pv_pending) {  // S overwrites the P that P V reads
+          if (!W.wait_warp(bar(Plan::kPFree + i), pvf_par)) return false;
+          pvf_par ^= 1;
+          pv_pending = false;
+          ptx::tc_fence_after();
         }
 #pragma unroll
         for (int h = 0; h < KP; ++h) {
@@ -1007,6 +1028,7 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
         if (needed) {
           ptx::tc_commit_warp(bar(Plan::kPFree + i));
           if (last) ptx::tc_commit_warp(bar(Plan::kOFull + i));
+          pv_pending = true;
         }
         return true;
       };
@@ -1024,6 +1046,14 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
         if (it.nbmax > 0) ok = do_S(mine(it.jlo));  // K(jlo); an empty item (packed batch) has no tiles
         if (ok && nb > 0 && nb - 1 == it.jlo) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last use of Q_i
         for (int j = it.jlo; j < it.nbmax && ok; ++j) {
+          if (C::kPAlias) {  // P(j) sits in S's columns: P(j) V(j) before S(j+1)
+            ok = do_PV(mine(j), j == lo, j == nb - 1);  // V(j)
+            if (ok && j + 1 < it.nbmax) {
+              ok = do_S(mine(j + 1));  // K(j+1)
+              if (ok && nb > 0 && j + 2 == nb) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last S_i
+            }
+            continue;
+          }
           if (j + 1 < it.nbmax) {
             ok = do_S(mine(j + 1));  // K(j+1)
             if (ok && nb > 0 && j + 2 == nb) ptx::tc_commit_warp(bar(Plan::kQEmpty + i));  // last S_i
@@ -1105,6 +1135,11 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
           const int hkv = it.h / p.kv_group;  // grouped-query attention: shared K/V head
           if (it.nbmax > 0) ok = fill(&tmK, it.jlo, hkv, it.tb, it.s0);
           for (int j = it.jlo; j < it.nbmax && ok; ++j) {
+            if (C::kPAlias) {  // the MMA warps' order: V(j), then K(j+1)
+              ok = fill(&tmV, j, hkv, it.tb, it.s0);
+              if (ok && j + 1 < it.nbmax) ok = fill(&tmK, j + 1, hkv, it.tb, it.s0);
+              continue;
+            }
             if (j + 1 < it.nbmax) ok = fill(&tmK, j + 1, hkv, it.tb, it.s0);
             if (ok) ok = fill(&tmV, j, hkv, it.tb, it.s0);
           }
