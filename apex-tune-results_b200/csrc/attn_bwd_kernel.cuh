@@ -46,10 +46,12 @@
 // from shared memory reads 8 KB, the shared-memory bandwidth of its 64 tensor cycles, so
 // every GEMM here is at least 128 wide in N.
 //
-// Warp roles (384 threads): warps 0-7 elementwise (warpgroup h handles columns
-// [64h, 64h + 64) of the 128 x 128 tile; thread = TMEM lane = row) and the per-item
-// epilogue; warp 8 issues every MMA (and owns TMEM); warp 9 schedules items and issues TMA;
-// warps 10-11 only give their registers to the elementwise warpgroups.
+// Warp roles (two-pass form, 640 threads): warps 0-15 elementwise (warpgroup w handles
+// columns [32w, 32w + 32) of the 128 x 128 tile; thread = TMEM lane = row) and the per-item
+// epilogue; warp 16 issues every MMA (and owns TMEM); warp 17 schedules items and issues
+// TMA; warps 18-19 only give their registers to the elementwise warpgroups. The fused form
+// has two elementwise warpgroups of 64 columns (warps 0-7), MMA warp 8, producer warp 9,
+// idle warps 10-11 and the dQ warps 12-15.
 #pragma once
 
 #include "attn_fwd_kernel.cuh"
@@ -65,6 +67,19 @@
 // pair: 0.621); at d = 128 one or two pairs are within run-to-run noise (6.74-6.82 ms).
 #ifndef APEX_BWD_EMU64
 #define APEX_BWD_EMU64 2
+#endif
+// Four elementwise warpgroups in the two-pass backward (see BwdCfg::kWG), with this many
+// registers each (the MMA/producer warpgroup gets 480 - 4 x this; 640 threads x 96). Off:
+// all backward tests pass with it, but it measured level (C2 0.598 vs 0.604-0.609 ms, C3
+// 6.24-6.27 vs 6.09-6.21 ms): the elementwise latency is not what paces the passes.
+#ifndef APEX_BWD_WG4
+#define APEX_BWD_WG4 0
+#endif
+#ifndef APEX_BWD_WG4_REGS
+#define APEX_BWD_WG4_REGS 104
+#endif
+#ifndef APEX_BWD_T2X2
+#define APEX_BWD_T2X2 0
 #endif
 #ifndef APEX_BWD_EMU128
 #define APEX_BWD_EMU128 0
@@ -112,20 +127,27 @@ struct BwdCfg {
   // two and a half steps (two tiles per step). The fused form gives 64 KB to the dS tile
   // and the dQ staging chunks.
   static constexpr int kNS = DQ ? (D == 64 ? 8 : 3) : (D == 64 ? 10 : 5);
-  // 12 warps: 8 elementwise, MMA, producer, 2 idle (+ 4 dQ warps in the fused form).
-  // Registers are granted per warpgroup, so the launch budget is kThreads x (65536 /
-  // kThreads); setmaxnreg moves it to the elementwise warpgroups (the split must not exceed
-  // the launch allocation, or setmaxnreg.inc would never return).
-  static constexpr int kThreads = DQ ? 512 : 384;
-  static constexpr int kWarpMma = 8;
-  static constexpr int kWarpProd = 9;
-  static constexpr int kWarpDq = 12;  // fused form: warps 12-15 reduce dQ tiles into global memory
+  // Elementwise warpgroups. Warpgroup w takes the tile's columns [kCols w, kCols (w + 1))
+  // for every row (thread = TMEM lane = row). The two-pass form runs four (32 columns
+  // each), so four elementwise warps share each SM sub-partition and hide each other's
+  // TMEM-load and math latency (the elementwise work is latency-bound: ~30 % issue with
+  // two). The fused form keeps two: its dQ warpgroup leaves no register room for four.
+  static constexpr int kWG = APEX_BWD_WG4 && !DQ ? 4 : 2;
+  static constexpr int kCols = 128 / kWG;
+  // Warps: the elementwise warpgroups, then MMA, producer, idle warps (+ 4 dQ warps in the
+  // fused form). Registers are granted per warpgroup, so the launch budget is kThreads x
+  // (65536 / kThreads); setmaxnreg moves it to the elementwise warpgroups (the split must
+  // not exceed the launch allocation, or setmaxnreg.inc would never return).
+  static constexpr int kThreads = 128 * (kWG + 1) + (DQ ? 128 : 0);
+  static constexpr int kWarpMma = 4 * kWG;
+  static constexpr int kWarpProd = kWarpMma + 1;
+  static constexpr int kWarpDq = kWarpMma + 4;  // fused form: 4 warps reduce dQ tiles into global memory
   // Fused splits: the ones without spills in the plain (unwindowed, batched) builds.
-  static constexpr int kRegsElementwise = DQ ? 200 : 224;
-  static constexpr int kRegsOther = DQ && D == 64 ? 48 : 56;
+  static constexpr int kRegsElementwise = kWG == 4 ? APEX_BWD_WG4_REGS : (DQ ? 200 : 224);
+  static constexpr int kRegsOther = kWG == 4 ? 480 - 4 * APEX_BWD_WG4_REGS : (DQ && D == 64 ? 48 : 56);
   static constexpr int kRegsDq = DQ ? (D == 64 ? 64 : 56) : 0;
   static constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
-  static_assert(128 * (2 * kRegsElementwise + kRegsOther + kRegsDq) <= kThreads * kLaunchRegs,
+  static_assert(128 * (kWG * kRegsElementwise + kRegsOther + kRegsDq) <= kThreads * kLaunchRegs,
                 "setmaxnreg split exceeds the launch register allocation");
   // TMEM columns: T1 scores, T2 dP (then packed P / dS), Acc1 dK | dQ, Acc2 dV (KV pass),
   // XQ / XdO the item's Q and dO as 16-bit pairs (Q pass).
@@ -135,6 +157,13 @@ struct BwdCfg {
   static constexpr int kAcc2 = 256 + D;
   static constexpr int kXQ = 256 + D;
   static constexpr int kXdO = kXQ + D / 2;
+  // Two-pass form at d = 64 (APEX_BWD_T2X2): a second T2 buffer in the 128 free columns
+  // [384, 512), used by odd steps, so the dP GEMM of step s waits only for the accumulating
+  // GEMMs of step s - 2. Off: all backward tests pass with it, but C2 measured 3 % slower
+  // (0.623 vs 0.603 ms): the P / dS hand-off through T2 is not what paces the passes.
+  static constexpr int kT2Bufs = D == 64 && !DQ && APEX_BWD_T2X2 ? 2 : 1;
+  static constexpr int kT2b = 384;
+  static __host__ __device__ constexpr int t2_col(int b) { return b == 0 ? kT2 : kT2b; }
   // Fused form: the step's dQ tile (fp32, 128 query rows x D). At d = 64 two buffers fit
   // behind dV. At d = 128 TMEM is full: dQ borrows T2 once the step's dV and dK GEMMs have
   // read P and dS from it, and the next dP GEMM writes each 64-column half of T2 once the
@@ -147,6 +176,7 @@ struct BwdCfg {
                                       // the dQ warps' bulk_wait_group_read1 assumes 2
   static_assert(kAcc2 + D <= 512 && kXdO + D / 2 <= 512, "TMEM plan overflows 512 columns");
   static_assert(!DQ || kDqInT2 || kDq + kDqBufs * D <= 512, "dQ buffers overflow TMEM");
+  static_assert(kT2Bufs == 1 || (kAcc2 + D <= kT2b && kXdO + D / 2 <= kT2b), "second T2 buffer overlaps");
 };
 
 template <int D, bool DQ = false>
@@ -179,10 +209,11 @@ struct BwdSmem {
   static constexpr int kXTFree = kXTFull + 1;   // Q pass: last MMA reading TMEM X done
   static constexpr int kT1Full = kXTFree + 1;
   static constexpr int kT1Free = kT1Full + 1;   // elementwise warps hold S in registers
-  static constexpr int kT2Full = kT1Free + 1;   // [2] dP of column half h
-  static constexpr int kT2Free = kT2Full + 2;   // [2] accumulating GEMMs of half h done
-  static constexpr int kPdSFull = kT2Free + 2;  // [2] P_h / dS_h packed in T2
-  static constexpr int kStatsFull = kPdSFull + 2;    // [2]
+  // [T2 buffer b][half h] at index 2 b + h:
+  static constexpr int kT2Full = kT1Free + 1;   // [4] dP of column half h
+  static constexpr int kT2Free = kT2Full + 4;   // [4] accumulating GEMMs of half h done
+  static constexpr int kPdSFull = kT2Free + 4;  // [4] P_h / dS_h packed in T2
+  static constexpr int kStatsFull = kPdSFull + 4;    // [2]
   static constexpr int kStatsEmpty = kStatsFull + 2;  // [2]
   static constexpr int kAccFull = kStatsEmpty + 2;
   static constexpr int kAccEmpty = kAccFull + 1;
@@ -409,26 +440,28 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
     ptx::mbar_init(bar(Plan::kXTFull), 256);
     ptx::mbar_init(bar(Plan::kXTFree), 1);
     ptx::mbar_init(bar(Plan::kT1Full), 1);
-    ptx::mbar_init(bar(Plan::kT1Free), 256);
-    for (int h = 0; h < 2; ++h) {
+    ptx::mbar_init(bar(Plan::kT1Free), 128 * C::kWG);
+    for (int h = 0; h < 4; ++h) {
       ptx::mbar_init(bar(Plan::kT2Full + h), 1);
       ptx::mbar_init(bar(Plan::kT2Free + h), 1);
-      ptx::mbar_init(bar(Plan::kPdSFull + h), 128);
+      ptx::mbar_init(bar(Plan::kPdSFull + h), 128 * (C::kWG / 2));  // the warpgroups of half h & 1
+    }
+    for (int h = 0; h < 2; ++h) {
       ptx::mbar_init(bar(Plan::kStatsFull + h), 1);
-      ptx::mbar_init(bar(Plan::kStatsEmpty + h), 256);
+      ptx::mbar_init(bar(Plan::kStatsEmpty + h), 128 * C::kWG);
     }
     ptx::mbar_init(bar(Plan::kAccFull), 1);
-    ptx::mbar_init(bar(Plan::kAccEmpty), 256);
+    ptx::mbar_init(bar(Plan::kAccEmpty), 128 * C::kWG);
     ptx::mbar_init(bar(Plan::kDrain), 1);
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar(Plan::kDqFull + b), 1);
       ptx::mbar_init(bar(Plan::kDqFree + b), 128);
     }
     ptx::mbar_init(bar(Plan::kDsFree), 1);
-    // Item-ring readers: the 8 elementwise warps, the MMA warp (and the 4 dQ warps).
+    // Item-ring readers: the elementwise warps, the MMA warp (and the 4 dQ warps).
     for (int k = 0; k < kItemRing; ++k) {
       ptx::mbar_init(bar(Plan::kItemFull + k), 1);
-      ptx::mbar_init(bar(Plan::kItemEmpty + k), DQ ? 13 : 9);
+      ptx::mbar_init(bar(Plan::kItemEmpty + k), 4 * C::kWG + 1 + (DQ ? 4 : 0));
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -453,15 +486,19 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
   if (warp < C::kWarpMma) {
     // ======================================================== elementwise ===
     ptx::setmaxnreg_inc<C::kRegsElementwise>();
+    constexpr int kCols = C::kCols;      // tile columns of this warpgroup
     const int quarter = warp & 3;
-    const int half = warp >> 2;          // column half of the 128 x 128 tile
+    const int wg = warp >> 2;            // elementwise warpgroup: columns [kCols wg, kCols (wg + 1))
+    const int half = wg / (C::kWG / 2);  // column half of the 128 x 128 tile
     const int r = quarter * 32 + lane;   // row (TMEM lane)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tT1 = tmem + lane_off + (uint32_t)(C::kT1 + 64 * half);
-    const uint32_t tT2 = tmem + lane_off + (uint32_t)(C::kT2 + 64 * half);
+    // T2: this warpgroup's kCols columns of dP, then its packed P (KV pass) and dS in place.
+    const uint32_t tT1 = tmem + lane_off + (uint32_t)(C::kT1 + kCols * wg);
+    const uint32_t tT2_0 = tmem + lane_off + (uint32_t)(C::t2_col(0) + kCols * wg);
+    const uint32_t tT2_1 = tmem + lane_off + (uint32_t)(C::t2_col(1) + kCols * wg);
     const float* stats = reinterpret_cast<const float*>(smem + Plan::kStats);
     const float c = p.scale_log2;
-    uint32_t t1_par = 0, t2_par = 0, af_par = 0, x_par = 0, xt_par = 0;
+    uint32_t t1_par = 0, af_par = 0, x_par = 0, xt_par = 0;
     int items_seen = 0;
     int gstep = 0;  // steps processed by this CTA
     bool ok = true;
@@ -480,6 +517,7 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         row_ndelta = p.ndelta[idx];
         // Copy the item's Q (warpgroup 0) or dO (warpgroup 1) row r from the swizzled
         // shared-memory tile into TMEM as 16-bit pairs: the A operand of the score GEMMs.
+        if (wg < 2) {
         if (!(ok = W.wait_warp(bar(Plan::kXFull), x_par))) break;
         x_par ^= 1;
         if (items_seen > 0) {  // the previous item's last score GEMMs read the TMEM copy
@@ -487,8 +525,8 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
           xt_par ^= 1;
           ptx::tc_fence_after();
         }
-        const uint32_t src = sbase + (half ? Plan::kX2 : Plan::kX1) + r * 128;
-        const uint32_t dst = tmem + lane_off + (uint32_t)(half ? C::kXdO : C::kXQ);
+        const uint32_t src = sbase + (wg ? Plan::kX2 : Plan::kX1) + r * 128;
+        const uint32_t dst = tmem + lane_off + (uint32_t)(wg ? C::kXdO : C::kXQ);
 #pragma unroll
         for (int cc = 0; cc < D / 64; ++cc) {
           uint32_t x[32];
@@ -506,13 +544,14 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(Plan::kXTFull));
         ptx::mbar_arrive(bar(Plan::kXEmpty));  // the shared-memory tiles may be refilled
+        }
       }
       ++items_seen;
       for (int s = 0; s < it.nsteps && ok; ++s, ++gstep) {
         const int ytile = it.lo + (KV ? s % nq : s);
         // KV pass: -lse2 / -delta of this step's query tile (double-buffered by step).
         const int sslot = gstep & 1;
-        const float* st_nlse = stats + sslot * 256 + 64 * half;
+        const float* st_nlse = stats + sslot * 256 + kCols * wg;
         const float* st_ndelta = st_nlse + 128;
         if (KV && !(ok = W.wait_warp(bar(Plan::kStatsFull + sslot), (uint32_t)(gstep >> 1) & 1u))) break;
         // Mask geometry: qi - kj = dq0 + (KV ? col - row : row - col).
@@ -523,24 +562,24 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         // sequence (not zero-filled) and are masked.
         const bool key_tail = VAR && !KV && !p.causal && (ytile + 1) * kBlockN > it.len;
         const bool masked = (p.causal && it_q == jb_k) || (WIN && dq0 + kBlockM - 1 > p.window) || key_tail;
-        const int colbase = 64 * half;
+        const int colbase = kCols * wg;
         if (!(ok = W.wait_warp(bar(Plan::kT1Full), t1_par))) break;
         t1_par ^= 1;
         ptx::tc_fence_after();
-        float pv[64];
+        float pv[kCols];
         {
-          uint32_t v[2][32];
-          ptx::tmem_ld32(tT1, v[0]);
-          ptx::tmem_ld32(tT1 + 32, v[1]);
+          uint32_t v[kCols / 32][32];
+#pragma unroll
+          for (int ch = 0; ch < kCols / 32; ++ch) ptx::tmem_ld32(tT1 + 32 * ch, v[ch]);
           ptx::tmem_wait_ld();
-          ptx::reg_fence32(v[0]);
-          ptx::reg_fence32(v[1]);
+#pragma unroll
+          for (int ch = 0; ch < kCols / 32; ++ch) ptx::reg_fence32(v[ch]);
           // S is in registers: the next score GEMM may overwrite T1.
           ptx::tc_fence_before();
           ptx::mbar_arrive(bar(Plan::kT1Free));
           if (KV) {
 #pragma unroll
-            for (int e = 0; e < 64; e += 4) {
+            for (int e = 0; e < kCols; e += 4) {
               const float4 l4 = *reinterpret_cast<const float4*>(st_nlse + e);
               const float2 x0 = __ffma2_rn(make_float2(__uint_as_float(v[e >> 5][e & 31]), __uint_as_float(v[e >> 5][(e & 31) + 1])),
                                            make_float2(c, c), make_float2(l4.x, l4.y));
@@ -554,7 +593,7 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
           } else {
             const float2 nl = make_float2(row_nlse2, row_nlse2);
 #pragma unroll
-            for (int e = 0; e < 64; e += 2) {
+            for (int e = 0; e < kCols; e += 2) {
               const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[e >> 5][e & 31]), __uint_as_float(v[e >> 5][(e & 31) + 1])),
                                           make_float2(c, c), nl);
               pv[e] = x.x;
@@ -564,7 +603,7 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         }
         if (masked) {
 #pragma unroll
-          for (int e = 0; e < 64; ++e) {
+          for (int e = 0; e < kCols; ++e) {
             const int dqk = dq0 + (KV ? colbase + e - r : r - colbase - e);
             if ((p.causal && dqk < 0) || (WIN && dqk > p.window) ||
                 (key_tail && ytile * kBlockN + colbase + e >= it.len))
@@ -573,10 +612,10 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         }
         if (masked || kEmu == 0) {
 #pragma unroll
-          for (int e = 0; e < 64; ++e) pv[e] = ptx::ex2(pv[e]);  // masked: exactly 0
+          for (int e = 0; e < kCols; ++e) pv[e] = ptx::ex2(pv[e]);  // masked: exactly 0
         } else {
 #pragma unroll
-          for (int e = 0; e < 64; e += 2) {
+          for (int e = 0; e < kCols; e += 2) {
             if (((e >> 1) & 7) < kEmu) {
               const float2 y = exp2_poly_pair(make_float2(pv[e], pv[e + 1]));
               pv[e] = y.x;
@@ -593,30 +632,38 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         // there, and causal masks hide such keys.)
         if (DQ && VAR && !p.causal && it.blk * kBlockN + r >= it.len) {
 #pragma unroll
-          for (int e = 0; e < 64; ++e) pv[e] = 0.f;
+          for (int e = 0; e < kCols; ++e) pv[e] = 0.f;
         }
-        uint32_t pk_p[32];
+        // kCols / 2 packed 16-bit pairs into this warpgroup's T2 columns.
+        auto st_packed = [&](uint32_t taddr, uint32_t (&w)[kCols / 2]) {
+          if constexpr (kCols == 64) ptx::tmem_st32(taddr, w);
+          else ptx::tmem_st16(taddr, w);
+        };
+        uint32_t pk_p[kCols / 2];
         if (KV) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) pk_p[e] = DType<T>::pack(pv[2 * e], pv[2 * e + 1]);
+          for (int e = 0; e < kCols / 2; ++e) pk_p[e] = DType<T>::pack(pv[2 * e], pv[2 * e + 1]);
         }
-        if (!(ok = W.wait_warp(bar(Plan::kT2Full + half), t2_par))) break;
-        t2_par ^= 1;
+        // T2 buffer of this step, and the parity of its use.
+        const int t2b = C::kT2Bufs == 2 ? (gstep & 1) : 0;
+        const uint32_t t2u = (uint32_t)(gstep / C::kT2Bufs) & 1u;
+        const uint32_t tT2 = t2b ? tT2_1 : tT2_0;
+        if (!(ok = W.wait_warp(bar(Plan::kT2Full + 2 * t2b + half), t2u))) break;
         ptx::tc_fence_after();
         {
-          uint32_t v[2][32];
-          ptx::tmem_ld32(tT2, v[0]);
-          ptx::tmem_ld32(tT2 + 32, v[1]);
+          uint32_t v[kCols / 32][32];
+#pragma unroll
+          for (int ch = 0; ch < kCols / 32; ++ch) ptx::tmem_ld32(tT2 + 32 * ch, v[ch]);
           ptx::tmem_wait_ld();
-          ptx::reg_fence32(v[0]);
-          ptx::reg_fence32(v[1]);
-          // dP is in registers; P_h goes into this warpgroup's first 32 T2 columns now, so
-          // its packed registers die before dS is formed.
-          if (KV) ptx::tmem_st32(tT2, pk_p);
-          uint32_t pk_s[32];
+#pragma unroll
+          for (int ch = 0; ch < kCols / 32; ++ch) ptx::reg_fence32(v[ch]);
+          // dP is in registers; P goes into this warpgroup's first kCols / 2 T2 columns
+          // now, so its packed registers die before dS is formed.
+          if (KV) st_packed(tT2, pk_p);
+          uint32_t pk_s[kCols / 2];
           if (KV) {
 #pragma unroll
-            for (int e = 0; e < 64; e += 4) {  // dS = P (dP - delta), two lanes per instruction
+            for (int e = 0; e < kCols; e += 4) {  // dS = P (dP - delta), two lanes per instruction
               const float4 d4 = *reinterpret_cast<const float4*>(st_ndelta + e);
               const float2 a01 = __fmul2_rn(make_float2(pv[e], pv[e + 1]),
                                             __fadd2_rn(make_float2(__uint_as_float(v[e >> 5][e & 31]), __uint_as_float(v[e >> 5][(e & 31) + 1])),
@@ -627,36 +674,37 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
               pk_s[e >> 1] = DType<T>::pack(a01.x, a01.y);
               pk_s[(e >> 1) + 1] = DType<T>::pack(a23.x, a23.y);
             }
-            ptx::tmem_st32(tT2 + 32, pk_s);  // dS_h after P_h
+            st_packed(tT2 + kCols / 2, pk_s);  // dS after P
             if (DQ) {
               // At d = 64 the previous step's dQ GEMM may still be reading the dS tile (it is
               // issued after this step's dP GEMM); at d = 128 it completed before dP (T2).
               if (!C::kDqInT2 && gstep > 0 && !(ok = W.wait_warp(bar(Plan::kDsFree), (uint32_t)(gstep - 1) & 1u)))
                 break;
-              // The same dS^T row into the shared-memory tile of the dQ GEMM: chunk `half`
-              // (queries 64 half ..), row r, 16-byte unit u at position u ^ (r & 7).
-              const uint32_t drow = sbase + Plan::kDs + half * Plan::kChunkBytes + r * 128;
+              // The same dS^T row into the shared-memory tile of the dQ GEMM: chunk
+              // colbase / 64 (64 queries each), row r, 16-byte unit u at position u ^ (r & 7).
+              const uint32_t drow = sbase + Plan::kDs + (uint32_t)(colbase / 64) * Plan::kChunkBytes + r * 128;
+              const uint32_t ub = (uint32_t)(colbase % 64) / 8;
 #pragma unroll
-              for (int u = 0; u < 8; ++u)
-                ptx::st_shared_v4(drow + (((uint32_t)u ^ (uint32_t)(r & 7)) << 4), pk_s[4 * u], pk_s[4 * u + 1],
+              for (int u = 0; u < kCols / 8; ++u)
+                ptx::st_shared_v4(drow + (((ub + (uint32_t)u) ^ (uint32_t)(r & 7)) << 4), pk_s[4 * u], pk_s[4 * u + 1],
                                   pk_s[4 * u + 2], pk_s[4 * u + 3]);
             }
             ptx::mbar_arrive(bar(Plan::kStatsEmpty + sslot));  // statistics read
           } else {
             const float2 nd = make_float2(row_ndelta, row_ndelta);
 #pragma unroll
-            for (int e = 0; e < 64; e += 2) {
+            for (int e = 0; e < kCols; e += 2) {
               const float2 a = __fmul2_rn(make_float2(pv[e], pv[e + 1]),
                                           __fadd2_rn(make_float2(__uint_as_float(v[e >> 5][e & 31]), __uint_as_float(v[e >> 5][(e & 31) + 1])), nd));
               pk_s[e >> 1] = DType<T>::pack(a.x, a.y);
             }
-            ptx::tmem_st32(tT2, pk_s);
+            st_packed(tT2, pk_s);
           }
           ptx::tmem_wait_st();
         }
         if (DQ) ptx::fence_proxy_async_smem();  // the dS tile, for the dQ GEMM
         ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(Plan::kPdSFull + half));
+        ptx::mbar_arrive(bar(Plan::kPdSFull + 2 * t2b + half));
       }
       if (!ok) break;
       // ---- epilogue: Acc1 * scale -> out1 (dK | dQ), Acc2 -> out2 (dV) ----
@@ -666,13 +714,15 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
       const int row = it.blk * kBlockM + r;
       const bool valid = row < it.len;
       constexpr int kHalfCols = D / 2;
-      auto store = [&](void* base, long long sb, long long sh, long long sn, int acc_col, float scale) {
+      // Half `hh` of the columns of one accumulator. Two warpgroups: warpgroup h stores half
+      // h of each; four: warpgroups 0, 1 the halves of Acc1, warpgroups 2, 3 those of Acc2.
+      auto store = [&](void* base, long long sb, long long sh, long long sn, int acc_col, float scale, int hh) {
         T* dst = reinterpret_cast<T*>(base) + (VAR ? 0LL : (long long)it.b * sb) + (long long)it.hx * sh +
-                 (long long)(it.s0 + row) * sn + half * kHalfCols;
+                 (long long)(it.s0 + row) * sn + hh * kHalfCols;
 #pragma unroll 1
         for (int ch = 0; ch < kHalfCols / 32; ++ch) {
           uint32_t v[32];
-          ptx::tmem_ld32(tmem + lane_off + (uint32_t)(acc_col + half * kHalfCols + ch * 32), v);
+          ptx::tmem_ld32(tmem + lane_off + (uint32_t)(acc_col + hh * kHalfCols + ch * 32), v);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v);
           uint32_t pk[16];
@@ -686,8 +736,14 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
           }
         }
       };
-      store(p.out1, p.o1_sb, p.o1_sh, p.o1_sn, C::kAcc1, p.out1_scale);
-      if (KV) store(p.out2, p.o2_sb, p.o2_sh, p.o2_sn, C::kAcc2, 1.f);
+      if (C::kWG == 2) {
+        store(p.out1, p.o1_sb, p.o1_sh, p.o1_sn, C::kAcc1, p.out1_scale, wg);
+        if (KV) store(p.out2, p.o2_sb, p.o2_sh, p.o2_sn, C::kAcc2, 1.f, wg);
+      } else if (wg < 2) {
+        store(p.out1, p.o1_sb, p.o1_sh, p.o1_sn, C::kAcc1, p.out1_scale, wg);
+      } else if (KV) {
+        store(p.out2, p.o2_sb, p.o2_sh, p.o2_sn, C::kAcc2, 1.f, wg - 2);
+      }
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar(Plan::kAccEmpty));
     }
@@ -724,14 +780,17 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         else ptx::umma_ts_warp(d_tmem, x_tmem + (uint32_t)(8 * kk), b0 + off, idesc, kk > 0 ? 1u : 0u);
       }
     };
-    // A: 128 x 64 16-bit operand packed in 32 TMEM columns at a_tmem; B: 64 rows x D.
+    // A: 128 x 64 16-bit operand packed in TMEM from a_tmem: 8 columns per 16 of its K
+    // (the tile's columns); B: 64 rows x D. With two elementwise warpgroups the 32 columns
+    // are contiguous; with four, each warpgroup's 16 sit at the start of its own 32 (then
+    // its dS), so K columns 32..63 start 32 TMEM columns in.
     auto gemm_acc = [&](uint32_t d_tmem, uint32_t a_tmem, uint32_t sB, bool accumulate) {
       const uint64_t b0 = make_sdesc_sw128(sB, Plan::kChunkBytes, 1024);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t boff = (uint32_t)(kk * 16 * 128) >> 4;
-        ptx::umma_ts_warp(d_tmem, a_tmem + (uint32_t)(8 * kk), b0 + boff, idAcc,
-                          (accumulate || kk > 0) ? 1u : 0u);
+        const uint32_t aoff = (uint32_t)(8 * kk + (C::kWG == 4 ? 16 * (kk >> 1) : 0));
+        ptx::umma_ts_warp(d_tmem, a_tmem + aoff, b0 + boff, idAcc, (accumulate || kk > 0) ? 1u : 0u);
       }
     };
     // Fused form: dQ(step) = dS K over the tile's 128 keys. A is the dS^T tile (rows = keys,
@@ -746,10 +805,14 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         ptx::umma_ss_warp(d_tmem, a0 + off, b0 + off, idDq, kk > 0 ? 1u : 0u);
       }
     };
-    const uint32_t tT1 = tmem + C::kT1, tT2 = tmem + C::kT2;
+    const uint32_t tT1 = tmem + C::kT1;
     const uint32_t tAcc1 = tmem + C::kAcc1, tAcc2 = tmem + C::kAcc2;
     Ring<NS> ring;
-    uint32_t x_par = 0, t1f_par = 0, t2f_par = 0, pds_par = 0, ae_par = 0;  // bit h: half h
+    uint32_t x_par = 0, t1f_par = 0, ae_par = 0;
+    // Step g uses T2 buffer g % kT2Bufs; its barriers' parity is that of the buffer's use
+    // count, g / kT2Bufs.
+    auto t2_buf = [](int g) { return C::kT2Bufs == 2 ? (g & 1) : 0; };
+    auto t2_use = [](int g) { return (uint32_t)(g / C::kT2Bufs) & 1u; };
     int steps_issued = 0, items_accumulated = 0;
     bool ok = true;
     struct Pending {
@@ -795,20 +858,20 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
       }
       const uint32_t sY1 = sRing + pd.st1 * Plan::kTileBytes;
       const uint32_t sY2 = sRing + pd.st2 * Plan::kTileBytes;
+      const int b = t2_buf(pd.g);
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
-        if (!W.wait_warp(bar(Plan::kPdSFull + h), (pds_par >> h) & 1u)) return false;
-        pds_par ^= 1u << h;
+        if (!W.wait_warp(bar(Plan::kPdSFull + 2 * b + h), t2_use(pd.g))) return false;
         ptx::tc_fence_after();
         const bool acc = !pd.first || h > 0;
-        const uint32_t tP = tT2 + (uint32_t)(64 * h);
+        const uint32_t tP = tmem + (uint32_t)(C::t2_col(b) + 64 * h);
         if (KV) {
           gemm_acc(tAcc2, tP, sY2 + h * kHalfRows, acc);       // dV += P_h^T dO_h
-          gemm_acc(tAcc1, tP + 32, sY1 + h * kHalfRows, acc);  // dK += dS_h^T Q_h
+          gemm_acc(tAcc1, tP + C::kCols / 2, sY1 + h * kHalfRows, acc);  // dK += dS_h^T Q_h
         } else {
           gemm_acc(tAcc1, tP, sY1 + h * kHalfRows, acc);       // dQ += dS_h K_h
         }
-        ptx::tc_commit_warp(bar(Plan::kT2Free + h));
+        ptx::tc_commit_warp(bar(Plan::kT2Free + 2 * b + h));
       }
       // The step's Q and dO tiles are not read after dK and dV.
       ptx::tc_commit_warp(bar(Plan::kRingEmpty + pd.st1));
@@ -820,10 +883,8 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
       if constexpr (C::kDqInT2) {
         // dQ overwrites T2: wait until the dV and dK GEMMs above have read P and dS there.
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          if (!W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u)) return false;
-          t2f_par ^= 1u << h;
-        }
+        for (int h = 0; h < 2; ++h)
+          if (!W.wait_warp(bar(Plan::kT2Free + h), t2_use(pd.g))) return false;
         ptx::tc_fence_after();
         return issue_dq(pd);
       }
@@ -869,39 +930,39 @@ __global__ void __launch_bounds__(BwdCfg<D, DQ>::kThreads, 1)
         if (kSplitDP) {
           // dP in two column halves: half h of T2 is rewritten as soon as A_h(s-1) finished
           // reading P_h / dS_h from it, and elementwise warpgroup h starts on it at once.
+          const int b = t2_buf(steps_issued);
 #pragma unroll 1
           for (int h = 0; h < 2 && ok; ++h) {
-            if (steps_issued > 0) {
+            if (steps_issued >= C::kT2Bufs) {
               if (C::kDqInT2) {  // the dQ warps read this half of dQ(s-1) out of T2
                 if (!(ok = W.wait_warp(bar(Plan::kDqFree + h), (uint32_t)(steps_issued - 1) & 1u))) break;
-              } else {
-                if (!(ok = W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u))) break;
-                t2f_par ^= 1u << h;
+              } else {  // the accumulating GEMMs of the buffer's previous step are done
+                if (!(ok = W.wait_warp(bar(Plan::kT2Free + 2 * b + h), t2_use(steps_issued - C::kT2Bufs)))) break;
               }
               ptx::tc_fence_after();
             }
-            gemm_nt(tT2 + (uint32_t)(64 * h), sX2, tmem + C::kXdO,
+            gemm_nt(tmem + (uint32_t)(C::t2_col(b) + 64 * h), sX2, tmem + C::kXdO,
                     sRing + st2 * Plan::kTileBytes + h * kHalfRows, idNT64);
-            ptx::tc_commit_warp(bar(Plan::kT2Full + h));
+            ptx::tc_commit_warp(bar(Plan::kT2Full + 2 * b + h));
           }
           if (!ok) break;
         } else {
-          if (steps_issued > 0) {
+          const int b = t2_buf(steps_issued);
+          if (steps_issued >= C::kT2Bufs) {
 #pragma unroll 1
             for (int h = 0; h < 2 && ok; ++h) {
               if (C::kDqInT2) {
                 ok = W.wait_warp(bar(Plan::kDqFree + h), (uint32_t)(steps_issued - 1) & 1u);
               } else {
-                ok = W.wait_warp(bar(Plan::kT2Free + h), (t2f_par >> h) & 1u);
-                t2f_par ^= 1u << h;
+                ok = W.wait_warp(bar(Plan::kT2Free + 2 * b + h), t2_use(steps_issued - C::kT2Bufs));
               }
             }
             if (!ok) break;
             ptx::tc_fence_after();
           }
-          gemm_nt(tT2, sX2, tmem + C::kXdO, sRing + st2 * Plan::kTileBytes, idNT);
-          ptx::tc_commit_warp(bar(Plan::kT2Full));
-          ptx::tc_commit_warp(bar(Plan::kT2Full + 1));
+          gemm_nt(tmem + (uint32_t)C::t2_col(b), sX2, tmem + C::kXdO, sRing + st2 * Plan::kTileBytes, idNT);
+          ptx::tc_commit_warp(bar(Plan::kT2Full + 2 * b));
+          ptx::tc_commit_warp(bar(Plan::kT2Full + 2 * b + 1));
         }
         if (dq_next.valid && !(ok = issue_dq(dq_next))) break;
         if (!KV) ptx::tc_commit_warp(bar(Plan::kRingEmpty + st2));  // V: only dP reads it
