@@ -81,11 +81,14 @@ struct AttnParams {
 #ifndef APEX_FWD_CS64
 #define APEX_FWD_CS64 2
 #endif
-// Row-split softmax at d = 128 too (two warpgroups per sub-tile, P stored to shared memory
-// by 4-byte words). Off: measured level with one warpgroup per sub-tile (fp16 MLS d128
-// 1164 vs 1164 TFLOP/s, C3 within noise), so d = 128 is not limited by softmax latency.
+// Row-split softmax at d = 128 too: two warpgroups per sub-tile, so four softmax warps share
+// each SM sub-partition and overlap one another's exponential phases. P goes to the shared-
+// memory P tile with stmatrix (the 16-lane TMEM fragment is the stmatrix fragment). On:
+// C3 +1-3.5 % and the fp16 MLS d=128 shape +1-10 % over one warpgroup per sub-tile
+// (alternating builds, both orders). With 4-byte P stores instead of stmatrix it measured
+// level.
 #ifndef APEX_FWD_ROWSPLIT128
-#define APEX_FWD_ROWSPLIT128 0
+#define APEX_FWD_ROWSPLIT128 1
 #endif
 
 // d = 128: P written into TMEM over the first 64 columns of its own S (instead of a shared-
@@ -534,8 +537,7 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
       const uint32_t tP = tmem + lane_off + (uint32_t)(C::kTmemP + i * C::kPStride);
       // P in shared memory (d = 128): the SW128 K-major tile of the sub-tile, keys 0-63 and
       // 64-127 in two 16 KB chunks; 16-byte unit u of row R sits at unit position
-      // u ^ (R & 7). This thread writes the 4-byte word (lane % 4) of its units.
-      const uint32_t sP = sbase + Plan::kP + i * Plan::kPTileBytes + (uint32_t)(lane & 3) * 4;
+      // u ^ (R & 7) (stored with stmatrix below).
       const float c = p.scale_log2;
       const float2 c2 = make_float2(c, c);
       uint32_t s_par = 0, le_par = 1, pf_par = 0;
@@ -661,15 +663,20 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
           if constexpr (C::kPInTmem) {
             ptx::tmem_st_16x128b_x16(tP, pk);
           } else {
+            // pk[m], m = 2e + rr, is this thread's pair of the 8 x 8 block (rows lb + 8rr ..,
+            // keys 8e ..) in exactly the stmatrix fragment layout (row lane / 4, columns
+            // 2 (lane % 4) ..). Eight stmatrix.x4 store the warp's 16 rows: matrix m of
+            // instruction k is 4k + lane / 8, and this lane gives the address of its row
+            // lane % 8 (16-byte unit e % 8 of the row, swizzled, in 64-key chunk e / 8).
+            const uint32_t sP0 = sbase + Plan::kP + i * Plan::kPTileBytes;
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-              const int row = ra + 8 * rr;
-              const uint32_t rowp = sP + (uint32_t)row * 128;
-#pragma unroll
-              for (int e = 0; e < 16; ++e)
-                ptx::st_shared_b32(rowp + (uint32_t)(e >> 3) * Plan::kChunkBytes +
-                                       (((uint32_t)(e & 7) ^ (uint32_t)(row & 7)) << 4),
-                                   pk[2 * e + rr]);
+            for (int k = 0; k < 8; ++k) {
+              const int m = 4 * k + (lane >> 3);
+              const int e = m >> 1;
+              const int row = lb + 8 * (m & 1) + (lane & 7);
+              const uint32_t addr = sP0 + (uint32_t)(e >> 3) * Plan::kChunkBytes + (uint32_t)row * 128 +
+                                    (((uint32_t)(e & 7) ^ (uint32_t)(row & 7)) << 4);
+              ptx::stmatrix_x4(addr, pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
             }
             ptx::fence_proxy_async_smem();
           }
