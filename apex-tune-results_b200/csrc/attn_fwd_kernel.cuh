@@ -90,6 +90,11 @@ struct AttnParams {
 #ifndef APEX_FWD_ROWSPLIT128
 #define APEX_FWD_ROWSPLIT128 1
 #endif
+// The row split at d = 256 too (one sub-tile per CTA: two softmax warpgroups instead of one,
+// 512 threads). On: C4 +1.2 % (four alternating pairs, C4 timed alone); all forward tests pass.
+#ifndef APEX_FWD_ROWSPLIT256
+#define APEX_FWD_ROWSPLIT256 1
+#endif
 
 // d = 128: P written into TMEM over the first 64 columns of its own S (instead of a shared-
 // memory P buffer). Each sub-tile's next S then waits for its P V, and the freed 64 KB of
@@ -112,7 +117,8 @@ struct Cfg {
   // row max exchanged through shared memory and the row sums added in the epilogue (the
   // per-row window bounds do not fit the row split's register budget). The key split needs
   // P in TMEM, so windowed d = 128 launches keep one warpgroup per sub-tile.
-  static constexpr int kCS = D == 64 ? APEX_FWD_CS64 : ((D == 128 && !WIN && APEX_FWD_ROWSPLIT128) ? 2 : 1);
+  static constexpr int kCS = D == 64 ? APEX_FWD_CS64
+                            : ((!WIN && ((D == 128 && APEX_FWD_ROWSPLIT128) || (D == 256 && APEX_FWD_ROWSPLIT256))) ? 2 : 1);
   static constexpr bool kRowSplit = kCS == 2 && !WIN;
   static constexpr int kLSlots = kCS == 2 && !kRowSplit ? 2 : 1;  // row-sum slots per sub-tile
   static constexpr bool kPAlias = D == 128 && APEX_FWD_PALIAS128;  // P over S (see above)
@@ -130,9 +136,9 @@ struct Cfg {
   // setmaxnreg budgets (multiples of 8): softmax, epilogue, the remaining warpgroup. Their
   // sum x 128 must not exceed the launch allocation (kThreads x (65536 / kThreads)), or
   // setmaxnreg.inc would wait forever; checked below.
-  static constexpr int kRegsSoftmax = kCS == 2 ? (D == 128 ? 96 : 88) : (kSub == 2 ? 184 : 240);
-  static constexpr int kRegsEpilogue = kCS == 2 ? (D == 128 ? 56 : 64) : (kSub == 2 ? 80 : 128);
-  static constexpr int kRegsOther = kCS == 2 ? (D == 128 ? 40 : 48) : (kSub == 2 ? 56 : 136);
+  static constexpr int kRegsSoftmax = kCS == 2 ? (D == 128 ? 96 : (D == 256 ? 160 : 88)) : (kSub == 2 ? 184 : 240);
+  static constexpr int kRegsEpilogue = kCS == 2 ? (D == 128 ? 56 : (D == 256 ? 96 : 64)) : (kSub == 2 ? 80 : 128);
+  static constexpr int kRegsOther = kCS == 2 ? (D == 128 ? 40 : (D == 256 ? 96 : 48)) : (kSub == 2 ? 56 : 136);
   static constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
   static_assert(128 * (kSub * kCS * kRegsSoftmax + kRegsEpilogue + kRegsOther) <= kThreads * kLaunchRegs,
                 "setmaxnreg split exceeds the launch register allocation");
