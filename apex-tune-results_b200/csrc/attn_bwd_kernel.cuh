@@ -26,8 +26,9 @@
 // atomics from the dK/dV pass, trading 40% more tensor work for deterministic results and
 // no fp32 dQ scratch.
 // The fused mode (DQ = true) instead runs launch 2 with a fifth GEMM per step, dQ = dS K,
-// whose tiles warps 12-15 add into a zeroed fp32 accumulator with global reductions; a
-// cast kernel (attn_bwd_dq_cast_kernel) then writes dq = scale * acc.
+// whose tiles warps 12-15 add into a zeroed fp32 accumulator with TMA reduce-adds (staged
+// through shared memory); a cast kernel (attn_bwd_dq_cast_kernel) then writes
+// dq = scale * acc.
 //
 // TMEM and scheduling (both passes, 128 x 128 tiles, one CTA per SM):
 //   T1 [0, 128)     scores S^T | S (fp32). The elementwise warps read them into registers
@@ -46,12 +47,12 @@
 // from shared memory reads 8 KB, the shared-memory bandwidth of its 64 tensor cycles, so
 // every GEMM here is at least 128 wide in N.
 //
-// Warp roles (two-pass form, 640 threads): warps 0-15 elementwise (warpgroup w handles
-// columns [32w, 32w + 32) of the 128 x 128 tile; thread = TMEM lane = row) and the per-item
-// epilogue; warp 16 issues every MMA (and owns TMEM); warp 17 schedules items and issues
-// TMA; warps 18-19 only give their registers to the elementwise warpgroups. The fused form
-// has two elementwise warpgroups of 64 columns (warps 0-7), MMA warp 8, producer warp 9,
-// idle warps 10-11 and the dQ warps 12-15.
+// Warp roles (384 threads): warps 0-7 elementwise (warpgroup h handles columns
+// [64h, 64h + 64) of the 128 x 128 tile; thread = TMEM lane = row) and the per-item
+// epilogue; warp 8 issues every MMA (and owns TMEM); warp 9 schedules items and issues TMA;
+// warps 10-11 only give their registers to the elementwise warpgroups. The fused form adds
+// the dQ warps 12-15 (512 threads). APEX_BWD_WG4 (off) runs four elementwise warpgroups of
+// 32 columns instead (640 threads; MMA warp 16, producer warp 17).
 #pragma once
 
 #include "attn_fwd_kernel.cuh"
