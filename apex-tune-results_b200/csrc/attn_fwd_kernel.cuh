@@ -21,8 +21,11 @@
 //     "rescale-free" speed (fused_attention.py:61-82) without its overflow hazard for large
 //     logits.
 //
-// Warp roles (kSub = 2: d = 64, 128; kSub = 1: d = 256):
-//   warps [0, 4 kSub)           softmax, one warpgroup per query sub-tile (thread = row)
+// Warp roles (kSub = 2: d = 64, 128; kSub = 1: d = 256; kCS softmax warpgroups per
+// sub-tile, see Cfg):
+//   warps [0, 4 kSub kCS)       softmax: kCS warpgroups per query sub-tile; with kCS = 2
+//                               unwindowed launches split the sub-tile's rows between them
+//                               (16-lane TMEM shapes), windowed d = 64 ones its key columns
 //   next 4 warps                epilogue: O * (1/l) -> bf16/fp16 -> global, fp32 logsumexp
 //   next kSub warps             tcgen05.mma issuers (warp of sub-tile i; the first also
 //                               allocates TMEM)
@@ -110,13 +113,14 @@ template <int D, bool WIN = false>
 struct Cfg {
   static_assert(D == 64 || D == 128 || D == 256, "head dims 64, 128, 256");
   static constexpr int kSub = D == 256 ? 1 : 2;          // 128-row query sub-tiles per item
-  // Softmax warpgroups per sub-tile. Two per sub-tile put four softmax warps on every SM
-  // sub-partition, so one warp's loads, row max and P store overlap another's
-  // exponentials. Unwindowed launches split the sub-tile's rows between the two (kRowSplit:
-  // 16-lane TMEM shapes, nothing exchanged); windowed ones split its key columns, with the
-  // row max exchanged through shared memory and the row sums added in the epilogue (the
-  // per-row window bounds do not fit the row split's register budget). The key split needs
-  // P in TMEM, so windowed d = 128 launches keep one warpgroup per sub-tile.
+  // Softmax warpgroups per sub-tile. Two per sub-tile put more softmax warps on every SM
+  // sub-partition (four at d = 64 and 128), so one warp's loads, row max and P store overlap
+  // another's exponentials. Unwindowed launches split the sub-tile's rows between the two
+  // (kRowSplit: 16-lane TMEM shapes, nothing exchanged; all three head dims). Windowed
+  // d = 64 launches split its key columns instead, with the row max exchanged through
+  // shared memory and the row sums added in the epilogue (the per-row window bounds do not
+  // fit the row split's register budget). The key split needs P in TMEM, so windowed
+  // d = 128 and d = 256 launches keep one warpgroup per sub-tile.
   static constexpr int kCS = D == 64 ? APEX_FWD_CS64
                             : ((!WIN && ((D == 128 && APEX_FWD_ROWSPLIT128) || (D == 256 && APEX_FWD_ROWSPLIT256))) ? 2 : 1);
   static constexpr bool kRowSplit = kCS == 2 && !WIN;
