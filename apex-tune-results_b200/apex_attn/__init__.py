@@ -6,14 +6,14 @@ as the reference's nanochat model.
 """
 from .ops import (custom_attention_backward, custom_attention_forward,
                   custom_attention_varlen_backward, custom_attention_varlen_forward, device_status,
-                  selftest_wait_timeout, set_forward_kernel, supports_head_dim)
+                  forward_kernel_for, selftest_wait_timeout, set_forward_kernel, supports_head_dim)
 from . import _lib
 from . import torch_op  # registers torch.ops.apex_attn.fwd / .bwd
 from .torch_op import attention
 
 __all__ = ["attention", "custom_attention_forward", "custom_attention_backward",
            "custom_attention_varlen_forward", "custom_attention_varlen_backward", "device_status",
-           "selftest_wait_timeout", "set_forward_kernel", "supports_head_dim", "library_path", "version"]
+           "forward_kernel_for", "selftest_wait_timeout", "set_forward_kernel", "supports_head_dim", "library_path", "version"]
 
 
 def library_path() -> str:

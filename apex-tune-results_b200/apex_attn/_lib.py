@@ -106,6 +106,7 @@ SYMBOLS = {
                                                  ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "apex_attn_num_sms_hint": (ctypes.c_int, [ctypes.c_int]),
     "apex_attn_set_forward_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "apex_attn_forward_kernel_for": (ctypes.c_int, [ctypes.c_int] * 7),
     "apex_attn_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "apex_attn_noalloc_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "apex_attn_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p]),

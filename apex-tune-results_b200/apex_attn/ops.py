@@ -291,14 +291,27 @@ _FWD_KERNELS = {"auto": 0, "two_subtile": 1, "tile": 2}
 
 def set_forward_kernel(kind: str = "auto") -> None:
     """Selects the forward kernel for later calls in this process: "auto" (default: for
-    batched head dims 64 and 128 without a window, the kernel with the shorter estimated
-    makespan, which is the tile kernel only for problems too small to fill the GPU with
-    256-row items; the two-sub-tile kernel otherwise), "two_subtile" (that kernel
-    everywhere) or "tile" (the tile kernel wherever it applies). Both give results within
-    the operator's tolerance; this exists to measure them side by side."""
+    batched calls at head dim 128 without a window, the tile kernel when the call has
+    fewer than 3 x (SM count) 256-row query items, or N <= 2048 and fewer than 8 x (SM
+    count); the two-sub-tile kernel otherwise), "two_subtile" (that kernel everywhere) or
+    "tile" (the tile kernel wherever it applies). Both give results within the operator's
+    tolerance; this exists to measure them side by side."""
     if kind not in _FWD_KERNELS:
         raise ValueError(f"kind must be one of {sorted(_FWD_KERNELS)}, got {kind!r}")
     _lib.check(_lib.load().apex_attn_set_forward_kernel(_FWD_KERNELS[kind]), "set_forward_kernel")
+
+
+def forward_kernel_for(batch: int, heads: int, seq_len: int, head_dim: int, *, num_sms: int,
+                       window: int | None = None, packed: bool = False) -> str:
+    """Names the forward kernel ("tile" or "two_subtile") that a call of these dimensions
+    runs under the current selection on a device with `num_sms` SMs. For a packed batch,
+    `batch` is the sequence count and `seq_len` the longest sequence. Launches nothing."""
+    rc = _lib.load().apex_attn_forward_kernel_for(batch, heads, seq_len, head_dim,
+                                                   -1 if window is None else window,
+                                                   1 if packed else 0, num_sms)
+    if rc < 0:
+        _lib.check(rc, "forward_kernel_for")
+    return "tile" if rc == 2 else "two_subtile"
 
 
 def device_status(device: int | None = None) -> int:

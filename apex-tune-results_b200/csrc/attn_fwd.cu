@@ -371,12 +371,14 @@ int launch_tile(DeviceState& ds, unsigned attr_bit, const CUtensorMap& mq, const
 // both apply, automatic selection follows measurements on one B200 (bf16, causal):
 //   * the tile kernel runs a 128x128 tile slower per SM (0.64x at C2, d = 64; 0.82x at C3,
 //     d = 128: two softmax warps per SM sub-partition hide less latency than four);
-//   * its 128-row items double the parallelism. At d = 128 that wins while the problem
-//     has fewer than 4 x (SM count) 256-row items: B1 H8 N8192 1014 vs 798 TFLOP/s,
-//     B2 H8 N4096 901 vs 696, B1 H32 N1024 266 vs 245, B8 H32 N512 310 vs 279; at 512
-//     items (B2 H16 N4096) the two are level; at 1024 (B2 H16 N8192) the two-sub-tile
-//     kernel is 17 % faster. At d = 64 the tile kernel gains at most 8 % on small shapes
-//     and loses up to 14 %, so automatic selection keeps the two-sub-tile kernel.
+//   * its 128-row items double the parallelism. At d = 128 and N >= 4096 that wins while
+//     the problem has at most 384 256-row items (B1 H12 N8192 1111 vs 1054 TFLOP/s,
+//     B1 H8 N8192 1058 vs 855, B3 H8 N4096 955 vs 917) and loses from 448 (B1 H14 N8192
+//     1006 vs 1082, B2 H16 N4096 981 vs 1024, B2 H8 N8192 1076 vs 1172). At N <= 2048 the
+//     shorter causal rows keep it level or ahead up to about 1024 items (B6 H16 N2048 788
+//     vs 752 at 768 items, B8 H32 N1024 695 vs 662 at 1024, B8 H16 N2048 877 vs 874);
+//   * at d = 64 it gains at most 8 % on small shapes and loses up to 14 %, so automatic
+//     selection keeps the two-sub-tile kernel there.
 bool use_tile_kernel(int head_dim, const AttnParams& p, const CUtensorMap* mo, int num_sms) {
   const int kind = g_fwd_kind.load(std::memory_order_relaxed);
   if (kind == 1 || mo == nullptr || (head_dim != 64 && head_dim != 128) || p.window >= 0 ||
@@ -384,7 +386,7 @@ bool use_tile_kernel(int head_dim, const AttnParams& p, const CUtensorMap* mo, i
     return false;
   if (kind == 2) return true;
   const long long items = (long long)p.B * p.H * ((p.N + 2 * apex::kBlockM - 1) / (2 * apex::kBlockM));
-  return head_dim == 128 && items < 4LL * num_sms;
+  return head_dim == 128 && (items < 3LL * num_sms || (p.N <= 2048 && items < 8LL * num_sms));
 }
 
 // Validation, tensor maps, parameters and dispatch shared by both forward entry points.
@@ -1021,6 +1023,22 @@ int apex_attn_set_forward_kernel(int kind) {
   if (kind < 0 || kind > 2) return APEX_ATTN_ERR_INVALID_ARGUMENT;
   g_fwd_kind.store(kind, std::memory_order_relaxed);
   return APEX_ATTN_OK;
+}
+
+int apex_attn_forward_kernel_for(int batch, int heads, int seq_len, int head_dim, int window,
+                                 int packed, int num_sms) {
+  if (batch <= 0 || heads <= 0 || seq_len <= 0 || num_sms <= 0 || window < -1 ||
+      (head_dim != 64 && head_dim != 128 && head_dim != 256))
+    return APEX_ATTN_ERR_INVALID_ARGUMENT;
+  AttnParams p{};
+  p.B = batch;
+  p.H = heads;
+  p.N = seq_len;
+  p.window = window;
+  static const int kPackedMarker = 0;
+  p.cu_seqlens = packed ? &kPackedMarker : nullptr;
+  const CUtensorMap map{};
+  return use_tile_kernel(head_dim, p, packed ? nullptr : &map, num_sms) ? 2 : 1;
 }
 
 int apex_attn_num_sms_hint(int device) {

@@ -142,11 +142,11 @@ int apex_attn_fwd_varlen(const apex_attn_varlen_args* args, void* stream);
 
 /*
  * Selects the forward kernel for later calls in this process (all devices):
- *   0  automatic (default): for batched calls at head dims 64 and 128 without a window,
- *      whichever of the two kernels has the shorter estimated makespan: the tile kernel
- *      (one 128-row query tile per CTA, S and P double-buffered in tensor memory,
- *      TMA-store epilogue) for problems too small to fill the GPU with 256-row items,
- *      else the two-sub-tile kernel; the two-sub-tile kernel for every other call;
+ *   0  automatic (default): for batched calls at head dim 128 without a window, the tile
+ *      kernel (one 128-row query tile per CTA, S and P double-buffered in tensor memory,
+ *      TMA-store epilogue) when the call has fewer than 3 x (SM count) 256-row query
+ *      items (batch x heads x ceil(N / 256)), or N <= 2048 and fewer than 8 x (SM count);
+ *      the two-sub-tile kernel for every other call (measured crossovers on B200);
  *   1  the two-sub-tile kernel for every call;
  *   2  the tile kernel wherever it applies (batched, head dim 64 or 128, no window).
  * Both kernels compute the same function within the stated tolerances; this exists to
@@ -155,6 +155,18 @@ int apex_attn_fwd_varlen(const apex_attn_varlen_args* args, void* stream);
  * fused_attention.py:148-152).
  */
 int apex_attn_set_forward_kernel(int kind);
+
+/*
+ * Reports which forward kernel a call of these dimensions runs under the current
+ * selection (apex_attn_set_forward_kernel) on a device with `num_sms` SMs: 1 = the
+ * two-sub-tile kernel, 2 = the tile kernel. `window` is -1 for none; `packed` != 0 for a
+ * packed batch (apex_attn_fwd_varlen), whose `batch` is the sequence count and `seq_len`
+ * the longest sequence. Launches nothing and needs no device. Returns
+ * APEX_ATTN_ERR_INVALID_ARGUMENT for non-positive sizes or SM count, window < -1, or a
+ * head dim other than 64, 128 or 256. No counterpart in the reference.
+ */
+int apex_attn_forward_kernel_for(int batch, int heads, int seq_len, int head_dim, int window,
+                                 int packed, int num_sms);
 
 /*
  * Reads and clears the device status word of `device` after synchronising that

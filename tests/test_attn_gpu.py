@@ -396,6 +396,28 @@ def test_tile_kernel_is_deterministic_and_handles_fp16_gqa(fwd_kernel):
         check_ex_vs_oracle(2, 4, 2, 777, D, dtype="float16", seed=D + 1)
 
 
+def test_automatic_selection_runs_the_kernel_it_names(fwd_kernel):
+    """On each side of the d=128 item thresholds (3 x SMs at N=8192, 8 x SMs at N=2048),
+    the automatic output must be bit-identical to that of the kernel which
+    forward_kernel_for names for this device."""
+    import apex_attn
+    from apex_attn import custom_attention_forward
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    below_3 = (3 * sms - 1) // (8192 // 256)
+    below_8 = (8 * sms - 1) // (2048 // 256)
+    for bh, N, want in [(below_3, 8192, "tile"), (below_3 + 1, 8192, "two_subtile"),
+                        (below_8, 2048, "tile"), (below_8 + 1, 2048, "two_subtile")]:
+        assert apex_attn.forward_kernel_for(bh, 1, N, 128, num_sms=sms) == want, (bh, N)
+        q, k, v = (t.cuda() for t in make_inputs(bh, 1, N, 128, seed=bh + N))
+        outs = {}
+        for kind in ("auto", want):
+            fwd_kernel(kind)
+            outs[kind] = custom_attention_forward(q, k, v)
+        torch.cuda.synchronize()
+        assert torch.equal(outs["auto"], outs[want]), (bh, N, want)
+        del q, k, v, outs
+
+
 def test_set_forward_kernel_rejects_unknown_kind():
     import apex_attn
     with pytest.raises(ValueError):

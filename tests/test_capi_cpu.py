@@ -316,3 +316,47 @@ def test_num_sms_hint_without_device(lib):
         pytest.skip("checks the no-device path")
     assert lib.apex_attn_num_sms_hint(0) == _lib.ERR_NO_DEVICE
     assert lib.apex_attn_num_sms_hint(-1) == _lib.ERR_NO_DEVICE
+
+
+@pytest.mark.parametrize("B,H,N,D,window,packed,want", [
+    # d=128, N >= 4096: the tile kernel below 3 x 148 = 444 256-row items
+    (1, 13, 8192, 128, -1, 0, 2),    # 416 items
+    (1, 14, 8192, 128, -1, 0, 1),    # 448
+    (3, 8, 4096, 128, -1, 0, 2),     # 384
+    (2, 16, 4096, 128, -1, 0, 1),    # 512
+    (4, 32, 8192, 128, -1, 0, 1),    # C3: 4096
+    # d=128, N <= 2048: below 8 x 148 = 1184 items
+    (147, 1, 2048, 128, -1, 0, 2),   # 1176
+    (148, 1, 2048, 128, -1, 0, 1),   # 1184
+    (8, 32, 1024, 128, -1, 0, 2),    # 1024
+    (16, 32, 1024, 128, -1, 0, 1),   # 2048
+    (8, 32, 512, 128, -1, 0, 2),     # 512 (N=512 rounds up to 2 items per head)
+    # the two-sub-tile kernel for d=64 and d=256, windows and packed batches
+    (1, 8, 2048, 64, -1, 0, 1),
+    (1, 1, 256, 256, -1, 0, 1),
+    (1, 8, 2048, 128, 256, 0, 1),
+    (1, 8, 2048, 128, -1, 1, 1),
+])
+def test_forward_kernel_selection(lib, B, H, N, D, window, packed, want):
+    assert lib.apex_attn_forward_kernel_for(B, H, N, D, window, packed, 148) == want
+
+
+def test_forward_kernel_selection_follows_pinning_and_validates(lib):
+    import apex_attn
+    try:
+        apex_attn.set_forward_kernel("two_subtile")
+        assert apex_attn.forward_kernel_for(1, 8, 2048, 128, num_sms=148) == "two_subtile"
+        apex_attn.set_forward_kernel("tile")
+        assert apex_attn.forward_kernel_for(4, 32, 8192, 128, num_sms=148) == "tile"
+        assert apex_attn.forward_kernel_for(4, 32, 8192, 64, num_sms=148) == "tile"
+        assert apex_attn.forward_kernel_for(1, 8, 2048, 256, num_sms=148) == "two_subtile"
+        assert apex_attn.forward_kernel_for(1, 8, 2048, 128, num_sms=148, window=64) == "two_subtile"
+        assert apex_attn.forward_kernel_for(1, 8, 2048, 128, num_sms=148, packed=True) == "two_subtile"
+    finally:
+        apex_attn.set_forward_kernel("auto")
+    assert apex_attn.forward_kernel_for(1, 8, 2048, 128, num_sms=148) == "tile"
+    for args in [(0, 1, 64, 128, -1, 0, 148), (1, 0, 64, 128, -1, 0, 148), (1, 1, 0, 128, -1, 0, 148),
+                 (1, 1, 64, 96, -1, 0, 148), (1, 1, 64, 128, -2, 0, 148), (1, 1, 64, 128, -1, 0, 0)]:
+        assert lib.apex_attn_forward_kernel_for(*args) == _lib.ERR_INVALID_ARGUMENT, args
+    with pytest.raises(RuntimeError):
+        apex_attn.forward_kernel_for(1, 1, 64, 96, num_sms=148)
