@@ -407,6 +407,7 @@ def test_automatic_selection_runs_the_kernel_it_names(fwd_kernel):
     below_8 = (8 * sms - 1) // (2048 // 256)
     for bh, N, want in [(below_3, 8192, "tile"), (below_3 + 1, 8192, "two_subtile"),
                         (below_8, 2048, "tile"), (below_8 + 1, 2048, "two_subtile")]:
+        fwd_kernel("auto")
         assert apex_attn.forward_kernel_for(bh, 1, N, 128, num_sms=sms) == want, (bh, N)
         q, k, v = (t.cuda() for t in make_inputs(bh, 1, N, 128, seed=bh + N))
         outs = {}
