@@ -551,6 +551,17 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
       const float c = p.scale_log2;
       const float2 c2 = make_float2(c, c);
       uint32_t s_par = 0, le_par = 1, pf_par = 0;
+      // P store addresses (d = 128), fixed per lane: stmatrix instruction k writes 16-byte
+      // unit e = 2k + lane / 16 of row R = lb + 8 ((lane / 8) % 2) + lane % 8, so its unit
+      // within the 64-key chunk k / 4 is (2 (k % 4) + lane / 16) ^ (R % 8), and R % 8 = lane % 8.
+      uint32_t p_row[4];
+      {
+        const uint32_t sP0 = sbase + Plan::kP + i * Plan::kPTileBytes;
+        const uint32_t row = (uint32_t)(lb + 8 * ((lane >> 3) & 1) + (lane & 7));
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          p_row[q] = sP0 + row * 128 + (((uint32_t)(2 * q + (lane >> 4)) ^ (uint32_t)(lane & 7)) << 4);
+      }
       int p_written = 0;  // P tiles handed over so far (the buffer is reused every tile)
       bool ok = true;
       ItemReader reader;
@@ -684,16 +695,12 @@ __global__ void __launch_bounds__(Cfg<D, WIN>::kThreads, 1)
             // keys 8e ..) in exactly the stmatrix fragment layout (row lane / 4, columns
             // 2 (lane % 4) ..). Eight stmatrix.x4 store the warp's 16 rows: matrix m of
             // instruction k is 4k + lane / 8, and this lane gives the address of its row
-            // lane % 8 (16-byte unit e % 8 of the row, swizzled, in 64-key chunk e / 8).
-            const uint32_t sP0 = sbase + Plan::kP + i * Plan::kPTileBytes;
+            // lane % 8: p_row[k & 3] in 64-key chunk k / 4 (the immediate offset).
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int m = 4 * k + (lane >> 3);
-              const int e = m >> 1;
-              const int row = lb + 8 * (m & 1) + (lane & 7);
-              const uint32_t addr = sP0 + (uint32_t)(e >> 3) * Plan::kChunkBytes + (uint32_t)row * 128 +
-                                    (((uint32_t)(e & 7) ^ (uint32_t)(row & 7)) << 4);
-              ptx::stmatrix_x4(addr, pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+            for (int k = 0; k < 4; ++k) {
+              ptx::stmatrix_x4<0>(p_row[k], pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+              ptx::stmatrix_x4<Plan::kChunkBytes>(p_row[k], pk[16 + 4 * k], pk[17 + 4 * k], pk[18 + 4 * k],
+                                                  pk[19 + 4 * k]);
             }
             ptx::fence_proxy_async_smem();
           }

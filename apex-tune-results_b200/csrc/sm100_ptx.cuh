@@ -347,9 +347,11 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 // Four 8 x 8 matrices of 16-bit elements to shared memory. For matrix j, lane t holds the
 // element pair (row t / 4, columns 2 (t % 4), 2 (t % 4) + 1) in register j, and lanes
 // 8j .. 8j + 7 give the 16-byte-aligned addresses of its rows 0 .. 7.
+// stmatrix.m8n8.x4 at shared address addr + OFF (OFF a compile-time byte offset).
+template <int OFF = 0>
 __device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
-  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
-               "r"(r2), "r"(r3)
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0+%5], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3), "n"(OFF)
                : "memory");
 }
 
