@@ -133,6 +133,74 @@ def test_bwd_vs_oracle(B, H, HKV, N, D, causal, win, dtype):
     assert_grads(got, ref, label + " e2e", atol=ATOL_E2E)
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("deterministic", [True, False])
+def test_bwd_score_ramp(D, causal, deterministic):
+    """Scores that grow by ~10 log2 units per 128-key tile (every row's softmax is carried
+    by its last ~20 keys, and lse reaches ~60): the backward recomputes P from lse with no
+    running max, so large lse values and underflowing early tiles must stay exact.
+
+    Here K reaches ~50-76 in one feature and dP = dO V^T ~ sqrt(D), so dq = scale * dS K
+    turns the 16-bit rounding of dS (before the dS K GEMM, as in every 16-bit attention
+    backward) into errors of several 1e-2; a fixed absolute tolerance does not fit. The
+    reference is float64 with the kernel's roundings (delta from the same bf16 O; dS and P
+    rounded to bf16 before their GEMMs), and the bound adds one bf16 ulp of every GEMM term:
+    2^-8 scale (|dS| |K|) for dq, 2^-8 scale (|dS|^T |Q|) for dk, 2^-8 (|P|^T |dO|) for dv.
+    A masking, delta or scheduling fault would miss it by orders of magnitude."""
+    from apex_attn import custom_attention_backward
+    g = torch.Generator().manual_seed(D + (3 if causal else 0))
+    N = 700
+    q = torch.randn(1, 2, N, D, generator=g) * 0.3
+    k = torch.randn(1, 2, N, D, generator=g) * 0.3
+    v = torch.randn(1, 2, N, D, generator=g)
+    do = torch.randn(1, 2, N, D, generator=g)
+    a = 8.0
+    b = 10.0 / (a * math.log2(math.e) / math.sqrt(D))
+    q[..., 0] += a
+    k[..., 0] = b * torch.arange(N, dtype=torch.float32) / 128.0
+    q, k, v, do = (t.to(torch.bfloat16) for t in (q, k, v, do))
+    o, lse = attention_np(*(t.float().numpy() for t in (q, k, v)), causal=causal)
+    got = custom_attention_backward(q.cuda(), k.cuda(), v.cuda(), torch.from_numpy(o).to(q.dtype).cuda(),
+                                    torch.from_numpy(lse).cuda(), do.cuda(), causal=causal,
+                                    deterministic=deterministic)
+    torch.cuda.synchronize()
+    o_rounded = torch.from_numpy(o).to(q.dtype).double().numpy()
+    ref, mag = _bwd_with_rounded_o(*(t.double().numpy() for t in (q, k, v, do)), o_rounded, causal)
+    for name, g_, r, m in zip(("dq", "dk", "dv"), got, ref, mag):
+        g_ = g_.float().cpu().numpy()
+        assert np.isfinite(g_).all()
+        excess = np.abs(g_ - r) / (ATOL + RTOL * np.abs(r) + 2.0 ** -8 * m)
+        assert excess.max() <= 1, f"ramp D{D} causal={causal} {name}: worst err/bound {excess.max():.2f}"
+
+
+def _bwd_with_rounded_o(q, k, v, do, o_rounded, causal):
+    """float64 attention gradients on [1, H, N, D] inputs with delta from a given (rounded)
+    O, and P and dS rounded to bf16 where the kernel rounds them (the scale is applied after
+    the dS GEMMs, as the kernel's epilogue does). Also returns, per gradient, the sum of the
+    magnitudes of its GEMM terms (|dS| |K| scale, |dS|^T |Q| scale, |P|^T |dO|)."""
+    def bf16(x):
+        return torch.from_numpy(x).to(torch.bfloat16).double().numpy()
+    _, H, N, D = q.shape
+    scale = 1.0 / math.sqrt(D)
+    hidden = np.triu(np.ones((N, N), dtype=bool), 1) if causal else np.zeros((N, N), dtype=bool)
+    out = [np.zeros_like(q) for _ in range(3)]
+    mag = [np.zeros_like(q) for _ in range(3)]
+    for h in range(H):
+        s = np.where(hidden, -np.inf, q[0, h] @ k[0, h].T * scale)
+        p = np.exp(s - s.max(axis=1, keepdims=True))
+        p /= p.sum(axis=1, keepdims=True)
+        delta = (do[0, h] * o_rounded[0, h]).sum(axis=1, keepdims=True)
+        ds = bf16(p * (do[0, h] @ v[0, h].T - delta))
+        out[0][0, h] = ds @ k[0, h] * scale
+        out[1][0, h] = ds.T @ q[0, h] * scale
+        out[2][0, h] = bf16(p).T @ do[0, h]
+        mag[0][0, h] = np.abs(ds) @ np.abs(k[0, h]) * scale
+        mag[1][0, h] = np.abs(ds).T @ np.abs(q[0, h]) * scale
+        mag[2][0, h] = p.T @ np.abs(do[0, h])
+    return tuple(x.astype(np.float32) for x in out), tuple(x.astype(np.float32) for x in mag)
+
+
 def _torch_fp32_grads(q, k, v, do, causal=True, window_left=None):
     """fp32 autograd of the explicit attention on the GPU (per head, no TF32)."""
     prev = torch.backends.cuda.matmul.allow_tf32

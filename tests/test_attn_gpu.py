@@ -396,6 +396,44 @@ def test_tile_kernel_is_deterministic_and_handles_fp16_gqa(fwd_kernel):
         check_ex_vs_oracle(2, 4, 2, 777, D, dtype="float16", seed=D + 1)
 
 
+def _ramp_inputs(B, H, N, D, direction, seed):
+    """q, k, v whose scores ramp along the keys by ~10 log2 units per 128-key tile
+    (direction +1: each row's max grows on every tile, so O and l rescale on every tile;
+    -1: the max sits in the first tile and later tiles underflow towards 0)."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, N, D, generator=g) * 0.3
+    k = torch.randn(B, H, N, D, generator=g) * 0.3
+    v = torch.randn(B, H, N, D, generator=g)
+    a = 8.0
+    c = math.log2(math.e) / math.sqrt(D)
+    b = 10.0 / (a * c)  # score growth per 128 keys, in score units
+    q[..., 0] += a
+    k[..., 0] = direction * b * torch.arange(N, dtype=torch.float32) / 128.0
+    return tuple(t.to(torch.bfloat16) for t in (q, k, v))
+
+
+@pytest.mark.parametrize("kind", ["two_subtile", "tile"])
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("direction", [1, -1])
+def test_score_ramp_rescales_every_tile(fwd_kernel, kind, D, causal, direction):
+    """Scores that grow by ~10 log2 units per key tile push every row's running max past the
+    2^8 rescale threshold on every tile (direction +1), so the O and row-sum rescale path
+    runs throughout; direction -1 keeps the first tile's max and underflows the rest."""
+    from apex_attn import custom_attention_forward
+    if kind == "tile" and D == 256:
+        pytest.skip("the tile kernel covers head dims 64 and 128")
+    fwd_kernel(kind)
+    q, k, v = _ramp_inputs(1, 2, 1000, D, direction, seed=D + (7 if causal else 0) + direction)
+    o, lse = custom_attention_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal, return_lse=True)
+    torch.cuda.synchronize()
+    ro, rl = attention_np(to_np32(q), to_np32(k), to_np32(v), causal=causal)
+    o = o.float().cpu().numpy()
+    assert np.isfinite(o).all()
+    assert np.abs(o - ro).max() <= O_TOL, np.abs(o - ro).max()
+    assert np.abs(lse.cpu().numpy() - rl).max() <= LSE_TOL, np.abs(lse.cpu().numpy() - rl).max()
+
+
 def test_automatic_selection_runs_the_kernel_it_names(fwd_kernel):
     """On each side of the d=128 item thresholds (3 x SMs at N=8192, 8 x SMs at N=2048),
     the automatic output must be bit-identical to that of the kernel which
