@@ -412,6 +412,23 @@ def _ramp_inputs(B, H, N, D, direction, seed):
     return tuple(t.to(torch.bfloat16) for t in (q, k, v))
 
 
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("direction", [1, -1])
+def test_score_ramp_with_window(D, direction):
+    """The ramp through the windowed kernels (keys split between two warpgroups, with a
+    per-tile row-max exchange): the window's newest keys carry every row."""
+    from apex_attn import custom_attention_forward
+    q, k, v = _ramp_inputs(1, 2, 1000, D, direction, seed=D + 11 + direction)
+    o, lse = custom_attention_forward(q.cuda(), k.cuda(), v.cuda(), causal=True, return_lse=True,
+                                      window_left=300)
+    torch.cuda.synchronize()
+    ro, rl = attention_np(to_np32(q), to_np32(k), to_np32(v), causal=True, window_left=300)
+    o = o.float().cpu().numpy()
+    assert np.isfinite(o).all()
+    assert np.abs(o - ro).max() <= O_TOL, np.abs(o - ro).max()
+    assert np.abs(lse.cpu().numpy() - rl).max() <= LSE_TOL, np.abs(lse.cpu().numpy() - rl).max()
+
+
 @pytest.mark.parametrize("kind", ["two_subtile", "tile"])
 @pytest.mark.parametrize("D", [64, 128, 256])
 @pytest.mark.parametrize("causal", [True, False])
