@@ -35,14 +35,15 @@ constexpr int kVersion = 300;  // 0.3.0
 // unmasked tile that use the FMA-pipe polynomial, per head dim. At d = 64 four softmax warps
 // share each sub-partition and leave issue slots free beside MUFU: one pair in eight on the
 // FMA pipe measured +4-5 % (C2 573-580 -> 601-604 TFLOP/s, fp16 MLS d64 651 -> 680); two
-// in eight the same, three in eight slower. At d = 128 two in eight measured +0.5 % at C3
-// and +1.4 % on the fp16 MLS d128 shape (builds alternating call by call in one process);
-// d = 256 is slower with any.
+// in eight the same, three in eight slower. At d = 128, with the row-split softmax and both
+// rows' max trees ahead of the rescale decisions, one in eight measures level to +2 % over
+// two (C3 and the fp16 MLS d128 shape, each timed first and second in alternating
+// processes); three in eight spills. d = 256 is slower with any.
 #ifndef APEX_EMU64
 #define APEX_EMU64 1
 #endif
 #ifndef APEX_EMU128
-#define APEX_EMU128 2
+#define APEX_EMU128 1
 #endif
 #ifndef APEX_EMU256
 #define APEX_EMU256 0
